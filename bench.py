@@ -1,0 +1,496 @@
+"""Benchmark of the MXFP8 x BF16 GEMM path (D = A*B + C) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload dense_projection|long_k|tall_skinny|wide|square|codec]
+
+One step is one pass of the hot path over one batch of synthetic input: one
+D = A*B + C call at the workload's shape (default: the dense projection
+M=4096, N=12288, K=4096), inputs resident in HBM.  The JSON line's ``value`` is
+whole-job TFLOP/s (2*M*N*K per GEMM, the reference's formula,
+include/gemm_common.h:30-37) over all ranks; ``e2e`` is the same metric through
+the C ABI with host buffers (pinned host -> device copies of A, B and C, the
+GEMM, device -> host copy of D, every step).
+
+Multi-GPU: one process per GPU (torchrun), each rank owns an independent
+M-slab of a GEMM whose total M is N_gpus x the per-rank M (weak scaling, no
+data-path collective; torch.distributed only for the barrier and the max over
+ranks of the timed region).
+
+``--impl reference`` times the reference's own CPU implementation of the path
+(gemm_reference_host + mxfp8_quantize_host from oracle/_ref, or the oracle's
+restatement when the reference was not built) on the host cores, on a bounded
+row sample of the same workload, extrapolated linearly in M (rows are
+independent).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "MXFP8×BF16 GEMM TFLOPS/GPU & % of BF16 TC peak at 1/2/4/8 B200"
+WORKLOADS = {
+    # name: (M per rank, N, K, seed)
+    "dense_projection": (4096, 12288, 4096, 43),
+    "long_k": (4096, 4096, 11008, 44),
+    "tall_skinny": (131072, 2048, 2048, 45),
+    "wide": (2048, 28672, 8192, 46),
+    "square": (16384, 16384, 16384, 46),
+}
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic(kernel: str, workload: str):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    p = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        d = json.load(f)
+    e = d.get(kernel, {}).get(workload)
+    return None if e is None else e.get("bytes_per_launch")
+
+
+# ----------------------------------------------------------------------------
+# clocks during the timed region
+# ----------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int, period_ms: int = 50):
+        self.gpu = gpu_index
+        self.period = period_ms
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", f"-lms={self.period}"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"],
+                    "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------
+# distributed plumbing
+# ----------------------------------------------------------------------------
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_dist(world: int, local: int):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return dist if world > 1 else None
+
+
+def barrier_sync(dist):
+    import torch
+
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(dist, value: float) -> float:
+    import torch
+
+    if dist is None:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------
+# CPU baseline: the reference's own host implementation on a bounded row sample
+# ----------------------------------------------------------------------------
+def cpu_baseline(M, N, K, seed, budget_s: float, threads: int | None = None):
+    """Times gemm_reference_host + mxfp8_quantize_host (the reference's CPU path
+    for D = MXFP8(A*B + C)) on a row sample, one row slab per host thread.
+    Returns (TFLOP/s extrapolated to the full workload, description dict)."""
+    import numpy as np
+
+    import oracle as O
+
+    threads = threads or O.default_threads()
+    kind = "reference" if O.ref_available() else "port"
+    rng = np.random.default_rng(seed)
+    B = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    B = O.bf16_bits_to_float(O.to_bf16_bits(B))
+    f32 = ctypes.POINTER(ctypes.c_float)
+    u8 = ctypes.POINTER(ctypes.c_uint8)
+
+    def run_rows(nrows_per_thread: int) -> float:
+        A = (rng.standard_normal((threads * nrows_per_thread, K)) * 0.02).astype(np.float32)
+        C = (rng.standard_normal((threads * nrows_per_thread, N)) * 0.02).astype(np.float32)
+        A = O.dequantize(*O.quantize(A))
+        C = O.dequantize(*O.quantize(C))
+        D = np.empty((A.shape[0], N), np.float32)
+        Dd = np.empty((A.shape[0], N), np.uint8)
+        Ds = np.empty((A.shape[0], (N + 31) // 32), np.uint8)
+
+        def work(t):
+            r0, r1 = t * nrows_per_thread, (t + 1) * nrows_per_thread
+            a, c, d = A[r0:r1], C[r0:r1], D[r0:r1]
+            if kind == "reference":
+                R = O.ref()
+                R.ref_gemm_reference_host(a.ctypes.data_as(f32), B.ctypes.data_as(f32),
+                                          c.ctypes.data_as(f32), d.ctypes.data_as(f32),
+                                          r1 - r0, N, K)
+                R.ref_mxfp8_quantize_host(d.ctypes.data_as(f32), Dd[r0:r1].ctypes.data_as(u8),
+                                          Ds[r0:r1].ctypes.data_as(u8), r1 - r0, N)
+            else:
+                d[...] = O.gemm_gold(a, B, c, threads=1)
+                Dd[r0:r1], Ds[r0:r1] = O.quantize(d, threads=1)
+
+        ths = [threading.Thread(target=work, args=(t,)) for t in range(threads)]
+        t0 = time.perf_counter()
+        for th in ths:
+            th.start()
+        for th in ths:
+            th.join()
+        return time.perf_counter() - t0
+
+    # calibrate with one row per thread, then size the sample to the budget
+    t1 = run_rows(1)
+    rows = max(1, min(64, int(budget_s / max(t1, 1e-3))))
+    if rows > 1:
+        t1 = run_rows(rows)
+    flops = 2.0 * threads * rows * N * K
+    tflops = flops / t1 / 1e12
+    desc = {"value": tflops, "unit": "TFLOPS", "cores": threads, "kind": kind,
+            "sample": f"{threads * rows} rows x N={N} x K={K} ({threads} threads x {rows} rows, "
+                      f"{t1:.1f} s), extrapolated linearly in M to M={M}; "
+                      f"gemm_reference_host + mxfp8_quantize_host"}
+    return tflops, desc
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ----------------------------------------------------------------------------
+# our arm
+# ----------------------------------------------------------------------------
+def make_inputs(mpk, M, N, K, seed, rank):
+    """N(0, 0.02^2) sources drawn on the device, A and C quantized by the
+    library's codec along K and N, B cast to BF16 with RNE."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(seed * 1000 + rank)
+    A = torch.randn((M, K), generator=g, device="cuda") * 0.02
+    B = (torch.randn((K, N), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    C = torch.randn((M, N), generator=g, device="cuda") * 0.02
+    Ad, As = mpk.quantize(A)
+    Cd, Cs = mpk.quantize(C)
+    del A, C
+    D = torch.empty((M, N), dtype=torch.uint8, device="cuda")
+    Ds = torch.empty((M, (N + 31) // 32), dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    return Ad, As, B, Cd, Cs, D, Ds
+
+
+def run_gemm_arm(args, world, rank, local, dist):
+    import torch
+
+    import mix_precision_kernel_b200 as mpk
+
+    M, N, K, seed = WORKLOADS[args.workload]
+    Ad, As, B, Cd, Cs, D, Ds = make_inputs(mpk, M, N, K, seed, rank)
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+    L = mpk.lib()
+    a = [Ad.data_ptr(), As.data_ptr(), B.data_ptr(), Cd.data_ptr(), Cs.data_ptr(), D.data_ptr(),
+         Ds.data_ptr()]
+
+    def step():
+        rc = L.mpk_gemm_mxfp8_bf16(*a, M, N, K, sptr)
+        if rc:
+            raise mpk.MpkError(rc, L.mpk_last_error().decode())
+
+    for _ in range(args.warmup):
+        step()
+    barrier_sync(dist)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)  # let the sampler start before the timed region
+    barrier_sync(dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier_sync(dist)
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    assert mpk.device_status() == 0, "device wait expired"
+    ms_max = max_over_ranks(dist, ms)
+    flops = 2.0 * M * N * K
+    ms_per_step = ms_max / args.steps
+    value = world * flops * args.steps / (ms_max / 1e3) / 1e12
+    kernel_tflops = flops / (ms / args.steps / 1e3) / 1e12
+
+    # end to end through the C ABI with host buffers
+    hA = torch.empty_like(Ad, device="cpu").pin_memory(); hA.copy_(Ad)
+    hAs = torch.empty_like(As, device="cpu").pin_memory(); hAs.copy_(As)
+    hB = torch.empty_like(B, device="cpu").pin_memory(); hB.copy_(B)
+    hC = torch.empty_like(Cd, device="cpu").pin_memory(); hC.copy_(Cd)
+    hCs = torch.empty_like(Cs, device="cpu").pin_memory(); hCs.copy_(Cs)
+    hD = torch.empty_like(D, device="cpu").pin_memory()
+    hDs = torch.empty_like(Ds, device="cpu").pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (hA, hAs, hB, hC, hCs))
+    d2h = hD.numel() + hDs.numel()
+
+    def e2e_step():
+        Ad.copy_(hA, non_blocking=True); As.copy_(hAs, non_blocking=True)
+        B.copy_(hB, non_blocking=True); Cd.copy_(hC, non_blocking=True)
+        Cs.copy_(hCs, non_blocking=True)
+        step()
+        hD.copy_(D, non_blocking=True); hDs.copy_(Ds, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        e2e_step()
+    barrier_sync(dist)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier_sync(dist)
+    e2e_ms = max_over_ranks(dist, e0.elapsed_time(e1))
+    e2e_value = world * flops * e2e_steps / (e2e_ms / 1e3) / 1e12
+
+    peaks, peak_src = load_peaks()
+    peak = float(peaks["bf16_tflops"])
+    roofline = {"bound": "tensor", "achieved": round(kernel_tflops, 2), "peak": peak,
+                "unit": "TFLOP/s", "frac": round(kernel_tflops / peak, 4),
+                "traffic": load_traffic("gemm_mxfp8_bf16_kernel", args.workload),
+                "peak_source": f"{peak_src} bf16_tflops (burst; kernel timed back to back)",
+                "algorithmic": f"2*M*N*K = {flops:.4e} FLOP per launch"}
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (N(0,0.02^2) drawn on device, torch Philox seeded; A/C quantized to "
+                "MXFP8 by the library, B rounded to BF16)",
+        "config": {"workload": f"{args.workload} GEMM D=A*B+C", "M_per_gpu": M, "M_total": M * world,
+                   "N": N, "K": K, "A": "MXFP8 e4m3+e8m0/32 along K", "B": "bf16 [K][N]",
+                   "C": "MXFP8 along N", "D": "MXFP8 along N", "seed": seed,
+                   "parallelism": f"M-slab x{world}, no collective",
+                   "l2": f"inputs+outputs {((M*K*33)//32 + 2*K*N + 2*(M*N*33)//32)/2**20:.0f} MiB > "
+                         f"126 MiB L2; no flush between steps"},
+        "gpu_launches": args.steps,
+        "pct_of_bf16_peak": round(100.0 * value / world / peak, 2),
+        "e2e": {"value": round(e2e_value, 3), "unit": "TFLOPS", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+        "roofline": roofline,
+        "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+    }
+    line["clocks"]["samples"] = clocks["samples"]
+    return line
+
+
+def run_codec_arm(args, world, rank, local, dist):
+    """Standalone MXFP8 quantize + dequantize of a 131072 x 2048 FP32 tensor
+    (HBM bandwidth kernels); value is GB/s of algorithmic traffic."""
+    import torch
+
+    import mix_precision_kernel_b200 as mpk
+
+    M, K = 131072, 2048
+    g = torch.Generator(device="cuda").manual_seed(45 + rank)
+    x = torch.randn((M, K), generator=g, device="cuda") * 0.02
+    d = torch.empty((M, K), dtype=torch.uint8, device="cuda")
+    s = torch.empty((M, K // 32), dtype=torch.uint8, device="cuda")
+    y = torch.empty_like(x)
+    L = mpk.lib()
+    sptr = torch.cuda.current_stream().cuda_stream
+    stream = torch.cuda.current_stream()
+    bytes_one = M * K * 4 + M * K + M * K // 32
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        barrier_sync(dist)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        barrier_sync(dist)
+        return e0.elapsed_time(e1) / args.steps
+
+    q_ms = timed(lambda: L.mpk_mxfp8_quantize(x.data_ptr(), d.data_ptr(), s.data_ptr(), M, K, sptr))
+    dq_ms = timed(lambda: L.mpk_mxfp8_dequantize(d.data_ptr(), s.data_ptr(), y.data_ptr(), M, K, sptr))
+    peaks, src = load_peaks()
+    hbm = float(peaks["hbm_gbs"])
+    qg, dg = bytes_one / q_ms / 1e6, bytes_one / dq_ms / 1e6
+    q_ms_max, dq_ms_max = max_over_ranks(dist, q_ms), max_over_ranks(dist, dq_ms)
+    value = world * bytes_one * 2 / ((q_ms_max + dq_ms_max) / 1e3) / 1e9
+    return {
+        "metric": "MXFP8 quantize+dequantize HBM GB/s (131072x2048 FP32)", "value": round(value, 1),
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(q_ms_max + dq_ms_max, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32/u8", "data": "synthetic N(0,0.02^2)",
+        "config": {"workload": "codec quantize+dequantize", "M": M, "K": K,
+                   "l2": "1 GiB FP32 tensor > L2"},
+        "gpu_launches": 2 * args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(qg, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(qg / hbm, 4), "traffic": load_traffic("mxfp8_quantize_flat_kernel", "codec"),
+                     "peak_source": f"{src} hbm_gbs", "dequantize_gbs": round(dg, 1),
+                     "dequantize_frac": round(dg / hbm, 4),
+                     "algorithmic": f"{bytes_one} B per launch (4 B in + 1 B + 1/32 B out per element)"},
+    }
+
+
+def run_reference_arm(args, world, rank):
+    if rank != 0:
+        return None
+    M, N, K, seed = WORKLOADS.get(args.workload, WORKLOADS["dense_projection"])
+    budget = float(os.environ.get("MPK_REF_STEP_BUDGET_S", "2.0"))
+    vals = []
+    desc = None
+    for i in range(args.warmup + args.steps):
+        v, desc = cpu_baseline(M, N, K, seed + i, budget)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.mean(vals)
+    desc = dict(desc, value=value)
+    desc["cpu_model"] = cpu_model()
+    return {
+        "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 2.0 * M * N * K / (value * 1e12) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic N(0,0.02^2)", "impl": "reference",
+        "config": {"workload": f"{args.workload} GEMM D=A*B+C", "M_per_gpu": M, "N": N, "K": K,
+                   "parallelism": "host threads, row slabs"},
+        "cpu_baseline": desc,
+        "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=list(WORKLOADS) + ["codec"], default="dense_projection")
+    ap.add_argument("--cpu-budget-s", type=float, default=12.0,
+                    help="seconds of host work for the cpu_baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_env()
+
+    if args.impl == "reference":
+        line = run_reference_arm(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    dist = init_dist(world, local)
+    try:
+        if args.workload == "codec":
+            line = run_codec_arm(args, world, rank, local, dist)
+        else:
+            line = run_gemm_arm(args, world, rank, local, dist)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload != "codec":
+            M, N, K, seed = WORKLOADS[args.workload]
+            _, desc = cpu_baseline(M, N, K, seed, args.cpu_budget_s)
+            desc["cpu_model"] = cpu_model()
+            line["cpu_baseline"] = desc
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,98 @@
+/*
+ * libmpk -- C ABI of the B200 (sm_100a) MXFP8 x BF16 GEMM and MXFP8 codec.
+ *
+ * Drop-in boundary for the hot path of chcoliang/mix_precision_kernel:
+ *
+ *     D = A * B + C
+ *     A  [M][K]  MXFP8: E4M3 codes (u8, row-major) + E8M0 scales (u8 [M][ceil(K/32)])
+ *     B  [K][N]  BF16, row-major (N contiguous)
+ *     C  [M][N]  MXFP8 with blocks along N (optional: both C pointers may be NULL)
+ *     D  [M][N]  MXFP8 with blocks along N
+ *
+ * Conventions (the reference's, include/gemm_kernels.h:7-9 and
+ * include/mxfp8_utils.h:24-47): scales are row-major [rows][ceil(cols/32)]
+ * indexed row*nblk + col/32; data is row-major with leading dimension cols; no
+ * padding or swizzle.  All pointers are device pointers owned by the caller.
+ * `stream` is a cudaStream_t (NULL = the legacy default stream).
+ *
+ * Differences from the reference, by design:
+ *   - every entry point returns a status code (0 = success) instead of calling
+ *     exit() on failure; a detail message is available from mpk_last_error();
+ *   - nothing allocates device memory: the launch path is stream-ordered, never
+ *     synchronizes the device and can be captured in a CUDA graph;
+ *   - indexing is 64-bit.
+ */
+#ifndef MPK_H_
+#define MPK_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  Values below 1000 are cudaError_t values passed through. */
+enum {
+    MPK_SUCCESS = 0,
+    MPK_ERR_INVALID_VALUE = 1001,   /* null pointer, negative size, size overflow */
+    MPK_ERR_UNSUPPORTED = 1002,     /* shape/stride the kernel does not handle (see mpk_status_string) */
+    MPK_ERR_MISALIGNED = 1003,      /* pointer alignment required by TMA not met */
+    MPK_ERR_DEVICE_TIMEOUT = 1004,  /* a bounded device-side wait expired (read by mpk_device_status) */
+    MPK_ERR_ARCH = 1005,            /* current device is not sm_100 */
+    MPK_ERR_DRIVER = 1006           /* CUDA driver entry point or tensor-map encoding failed */
+};
+
+/* D = A*B + C.  Replaces gemm_fp8_tensorcore (reference include/gemm_kernels.h:12-16,
+ * src/kernels/gemm_fp8_tensorcore.cu:231-249).  Requirements: K % 16 == 0 and
+ * N % 8 == 0 (TMA row strides), A_data and B 16-byte aligned.  C_data/C_scales
+ * may both be NULL (no C term).  Stream-ordered; allocates nothing. */
+int mpk_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
+                        const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
+                        uint8_t* D_scales, int M, int N, int K, void* stream);
+
+/* float [M][K] -> MXFP8 along K.  Replaces mxfp8_quantize_gpu (reference
+ * include/mxfp8_utils.h:38-40, src/quantize/mxfp8_quantize.cu:82-88).  Bit-exact
+ * with the reference's host and device quantizers.  Any K >= 1. */
+int mpk_mxfp8_quantize(const float* input, uint8_t* data, uint8_t* scales, int M, int K,
+                       void* stream);
+
+/* MXFP8 [M][K] -> float.  Replaces mxfp8_dequantize_gpu (reference
+ * include/mxfp8_utils.h:46-47, src/quantize/mxfp8_dequantize.cu:22-29).  Bit-exact. */
+int mpk_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, float* output, int M, int K,
+                         void* stream);
+
+/* Host-side utilities with the reference's semantics, for building inputs and
+ * checking results on the CPU (reference include/mxfp8_utils.h:34-35, :43-44;
+ * src/quantize/mxfp8_quantize.cu:116-144, src/quantize/mxfp8_dequantize.cu:32-47).
+ * Host pointers.  They are never used by the device entry points above. */
+int mpk_mxfp8_quantize_host(const float* input, uint8_t* data, uint8_t* scales, int M, int K);
+int mpk_mxfp8_dequantize_host(const uint8_t* data, const uint8_t* scales, float* output, int M,
+                              int K);
+
+/* Reads and clears the device-side status word of the current device after
+ * synchronizing it.  *device_status receives 0 when no bounded wait expired since
+ * the last read, else a nonzero site code; returns MPK_ERR_DEVICE_TIMEOUT in that
+ * case.  (The reference has no equivalent: its waits cannot fail.) */
+int mpk_device_status(int* device_status);
+
+/* Budget of every device-side spin wait, in nanoseconds (default 2e9). */
+int mpk_set_wait_timeout_ns(uint64_t ns);
+
+/* Launches one CTA that waits on an mbarrier nothing will arrive on, with the
+ * given budget; the wait must expire and record MPK_ERR_DEVICE_TIMEOUT in the
+ * device status word.  Exercises the timeout path without faulting the GPU. */
+int mpk_wait_selftest(uint64_t timeout_ns, void* stream);
+
+/* Static description of a status code, and the detail of the last failure on
+ * the calling thread. */
+const char* mpk_status_string(int status);
+const char* mpk_last_error(void);
+
+/* Library version (major*10000 + minor*100 + patch). */
+int mpk_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MPK_H_ */

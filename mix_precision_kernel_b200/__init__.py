@@ -1,0 +1,207 @@
+"""B200 (sm_100a) MXFP8 x BF16 GEMM and MXFP8 codec.
+
+Python binding of ``libmpk.so`` (C ABI in ``include/mpk.h``) through ctypes.
+The function names follow the reference project's C++ API
+(chcoliang/mix_precision_kernel ``include/gemm_kernels.h:12-16`` and
+``include/mxfp8_utils.h:34-47``) with the same argument order and meaning:
+
+    gemm_fp8_tensorcore(A_data, A_scales, B, C_data, C_scales, D_data, D_scales, M, N, K, stream)
+    mxfp8_quantize_gpu(input, data, scales, M, K, stream)
+    mxfp8_dequantize_gpu(data, scales, output, M, K, stream)
+    mxfp8_quantize_host(input, data, scales, M, K)
+    mxfp8_dequantize_host(data, scales, output, M, K)
+
+Arguments are torch CUDA tensors (or raw device addresses as ints) for the GPU
+functions and numpy arrays for the host functions.  Where the reference calls
+``exit()`` on a CUDA error, these raise :class:`MpkError`.  There is no CPU
+fallback: if ``libmpk.so`` is missing the import of any GPU function fails.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+__all__ = [
+    "MpkError", "lib", "library_path",
+    "gemm_fp8_tensorcore", "mxfp8_quantize_gpu", "mxfp8_dequantize_gpu",
+    "mxfp8_quantize_host", "mxfp8_dequantize_host",
+    "gemm", "quantize", "dequantize", "device_status", "set_wait_timeout_ns", "wait_selftest",
+    "MX_BLOCK", "nblk",
+]
+
+MX_BLOCK = 32
+_PKG = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_PKG, "_lib", "libmpk.so")
+_lock = threading.Lock()
+_lib = None
+
+MPK_SUCCESS = 0
+MPK_ERR_INVALID_VALUE = 1001
+MPK_ERR_UNSUPPORTED = 1002
+MPK_ERR_MISALIGNED = 1003
+MPK_ERR_DEVICE_TIMEOUT = 1004
+MPK_ERR_ARCH = 1005
+MPK_ERR_DRIVER = 1006
+
+
+class MpkError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"mpk status {status}: {message}")
+        self.status = status
+
+
+def nblk(cols: int) -> int:
+    return (cols + MX_BLOCK - 1) // MX_BLOCK
+
+
+def library_path() -> str:
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    """Load libmpk.so (built in-tree by ``mix_precision_kernel_b200.build``)."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(_LIB_PATH):
+                raise ImportError(
+                    f"{_LIB_PATH} is missing: build it with `python -m mix_precision_kernel_b200.build`")
+            L = ctypes.CDLL(_LIB_PATH)
+            vp, ci, u8p = ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p
+            L.mpk_gemm_mxfp8_bf16.argtypes = [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, vp]
+            L.mpk_mxfp8_quantize.argtypes = [vp, vp, vp, ci, ci, vp]
+            L.mpk_mxfp8_dequantize.argtypes = [vp, vp, vp, ci, ci, vp]
+            L.mpk_mxfp8_quantize_host.argtypes = [vp, u8p, u8p, ci, ci]
+            L.mpk_mxfp8_dequantize_host.argtypes = [u8p, u8p, vp, ci, ci]
+            L.mpk_device_status.argtypes = [ctypes.POINTER(ci)]
+            L.mpk_set_wait_timeout_ns.argtypes = [ctypes.c_uint64]
+            L.mpk_wait_selftest.argtypes = [ctypes.c_uint64, vp]
+            L.mpk_status_string.argtypes = [ci]
+            L.mpk_status_string.restype = ctypes.c_char_p
+            L.mpk_last_error.argtypes = []
+            L.mpk_last_error.restype = ctypes.c_char_p
+            for f in ("mpk_gemm_mxfp8_bf16", "mpk_mxfp8_quantize", "mpk_mxfp8_dequantize",
+                      "mpk_mxfp8_quantize_host", "mpk_mxfp8_dequantize_host", "mpk_device_status",
+                      "mpk_set_wait_timeout_ns", "mpk_wait_selftest", "mpk_version"):
+                getattr(L, f).restype = ci
+            _lib = L
+    return _lib
+
+
+def _check(status: int) -> None:
+    if status != MPK_SUCCESS:
+        L = lib()
+        detail = (L.mpk_last_error() or b"").decode(errors="replace")
+        msg = L.mpk_status_string(status).decode(errors="replace")
+        raise MpkError(status, f"{msg}; {detail}" if detail else msg)
+
+
+def _addr(t) -> int | None:
+    """Device address of a torch tensor, an int address, or None."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
+def _stream(stream, *tensors) -> int | None:
+    if stream is None:
+        for t in tensors:
+            if t is not None and not isinstance(t, int) and getattr(t, "is_cuda", False):
+                import torch
+                return torch.cuda.current_stream(t.device).cuda_stream
+        return None
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def _np_ptr(a):
+    import numpy as np
+    assert isinstance(a, np.ndarray) and a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+# ---------------------------------------------------------------------------
+# Reference-named entry points
+# ---------------------------------------------------------------------------
+
+def gemm_fp8_tensorcore(A_data, A_scales, B, C_data, C_scales, D_data, D_scales,
+                        M: int, N: int, K: int, stream=None) -> None:
+    """D = A*B + C (MXFP8 A, BF16 B [K][N], MXFP8 C/D along N).  C may be None."""
+    s = _stream(stream, A_data, D_data)
+    _check(lib().mpk_gemm_mxfp8_bf16(_addr(A_data), _addr(A_scales), _addr(B), _addr(C_data),
+                                     _addr(C_scales), _addr(D_data), _addr(D_scales), M, N, K, s))
+
+
+def mxfp8_quantize_gpu(input, data, scales, M: int, K: int, stream=None) -> None:
+    s = _stream(stream, input, data)
+    _check(lib().mpk_mxfp8_quantize(_addr(input), _addr(data), _addr(scales), M, K, s))
+
+
+def mxfp8_dequantize_gpu(data, scales, output, M: int, K: int, stream=None) -> None:
+    s = _stream(stream, data, output)
+    _check(lib().mpk_mxfp8_dequantize(_addr(data), _addr(scales), _addr(output), M, K, s))
+
+
+def mxfp8_quantize_host(input, data, scales, M: int, K: int) -> None:
+    _check(lib().mpk_mxfp8_quantize_host(_np_ptr(input), _np_ptr(data), _np_ptr(scales), M, K))
+
+
+def mxfp8_dequantize_host(data, scales, output, M: int, K: int) -> None:
+    _check(lib().mpk_mxfp8_dequantize_host(_np_ptr(data), _np_ptr(scales), _np_ptr(output), M, K))
+
+
+def device_status() -> int:
+    """Synchronize the current device, then read and clear its device status word."""
+    v = ctypes.c_int(0)
+    st = lib().mpk_device_status(ctypes.byref(v))
+    if st not in (MPK_SUCCESS, MPK_ERR_DEVICE_TIMEOUT):
+        _check(st)
+    return v.value
+
+
+def set_wait_timeout_ns(ns: int) -> None:
+    _check(lib().mpk_set_wait_timeout_ns(int(ns)))
+
+
+def wait_selftest(timeout_ns: int, stream=None) -> None:
+    _check(lib().mpk_wait_selftest(int(timeout_ns), _stream(stream)))
+
+
+# ---------------------------------------------------------------------------
+# Allocating conveniences (torch tensors)
+# ---------------------------------------------------------------------------
+
+def quantize(x, stream=None):
+    """float32 CUDA tensor [M, K] -> (codes uint8 [M, K], scales uint8 [M, ceil(K/32)])."""
+    import torch
+    assert x.dtype == torch.float32 and x.is_cuda and x.dim() == 2 and x.is_contiguous()
+    M, K = x.shape
+    d = torch.empty((M, K), dtype=torch.uint8, device=x.device)
+    s = torch.empty((M, nblk(K)), dtype=torch.uint8, device=x.device)
+    mxfp8_quantize_gpu(x, d, s, M, K, stream)
+    return d, s
+
+
+def dequantize(d, s, stream=None):
+    import torch
+    assert d.dtype == torch.uint8 and d.is_cuda and d.dim() == 2 and d.is_contiguous()
+    M, K = d.shape
+    out = torch.empty((M, K), dtype=torch.float32, device=d.device)
+    mxfp8_dequantize_gpu(d, s, out, M, K, stream)
+    return out
+
+
+def gemm(A_data, A_scales, B, C_data=None, C_scales=None, stream=None):
+    """Allocating form of :func:`gemm_fp8_tensorcore`; B is a bf16 CUDA tensor [K, N]."""
+    import torch
+    M, K = A_data.shape
+    K2, N = B.shape
+    assert K == K2 and B.dtype == torch.bfloat16 and B.is_contiguous()
+    D = torch.empty((M, N), dtype=torch.uint8, device=A_data.device)
+    Ds = torch.empty((M, nblk(N)), dtype=torch.uint8, device=A_data.device)
+    gemm_fp8_tensorcore(A_data, A_scales, B, C_data, C_scales, D, Ds, M, N, K, stream)
+    return D, Ds

@@ -1,0 +1,275 @@
+// extern "C" entry points of libmpk (declared in include/mpk.h): argument
+// validation, status codes, device checks and the host-side codec utilities.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "mpk.h"
+#include "mpk_internal.h"
+
+namespace mpk {
+
+namespace {
+thread_local char t_last_error[512] = "";
+std::mutex g_prop_mu;
+struct DevProps { bool init = false; int sms = 0, major = 0, minor = 0; };
+DevProps g_props[64];
+uint64_t g_timeout_ns = 2000000000ull;
+
+const DevProps& props()
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+    std::lock_guard<std::mutex> lk(g_prop_mu);
+    DevProps& p = g_props[dev];
+    if (!p.init) {
+        cudaDeviceGetAttribute(&p.sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaDeviceGetAttribute(&p.major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&p.minor, cudaDevAttrComputeCapabilityMinor, dev);
+        if (p.sms <= 0) p.sms = 148;
+        p.init = true;
+    }
+    return p;
+}
+}  // namespace
+
+void set_last_error(const char* fmt, ...)
+{
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+    va_end(ap);
+}
+
+int device_sm_count() { return props().sms; }
+int device_cc_major() { return props().major; }
+int device_cc_minor() { return props().minor; }
+uint64_t wait_timeout_ns() { return g_timeout_ns; }
+void set_wait_timeout_ns(uint64_t ns) { g_timeout_ns = ns; }
+
+static int check_arch()
+{
+    const DevProps& p = props();
+    if (p.major != 10 || p.minor != 0) {
+        set_last_error("libmpk is built for sm_100a; current device is sm_%d%d", p.major, p.minor);
+        return MPK_ERR_ARCH;
+    }
+    return MPK_SUCCESS;
+}
+
+static int from_cuda(cudaError_t e, const char* what)
+{
+    if (e == cudaSuccess) return MPK_SUCCESS;
+    set_last_error("%s: %s", what, cudaGetErrorString(e));
+    return (int)e;
+}
+
+// ---------------------------------------------------------------------------
+// Host-side codec (reference semantics; see include/mpk.h)
+// ---------------------------------------------------------------------------
+static inline uint32_t fbits(float f) { uint32_t u; std::memcpy(&u, &f, 4); return u; }
+static inline float bitsf(uint32_t u) { float f; std::memcpy(&f, &u, 4); return f; }
+
+static float host_e8m0_to_f32(uint8_t b) { return bitsf((uint32_t)b << 23); }
+
+static uint8_t host_e8m0_roundup(float x)
+{
+    if (x <= 0.0f) return 0;
+    const uint32_t u = fbits(x);
+    uint32_t e = (u >> 23) & 0xFFu;
+    if ((u & 0x7FFFFFu) && e < 255u) ++e;
+    return (uint8_t)e;
+}
+
+// Round-to-nearest-even into E4M3 after the reference's NaN test and clamp
+// (include/fp8_types.h:14-21).  Normal range: round the FP32 mantissa to 3 bits
+// with integer arithmetic; below 2^-6 the quantum is the fixed 2^-9.
+static uint8_t host_f32_to_e4m3(float x)
+{
+    if (std::isnan(x)) return 0x7F;
+    if (x > 448.0f) x = 448.0f;
+    if (x < -448.0f) x = -448.0f;
+    const uint32_t u = fbits(x);
+    const uint8_t sign = (uint8_t)((u >> 24) & 0x80u);
+    const uint32_t a = u & 0x7FFFFFFFu;
+    if (a >= 0x3C800000u) {  // |x| >= 2^-6
+        const uint32_t r = a + 0x7FFFFu + ((a >> 20) & 1u);
+        const uint32_t e = (r >> 23) - 120u;  // rebias 127 -> 7
+        return sign | (uint8_t)((e << 3) | ((r >> 20) & 7u));
+    }
+    const float q = std::nearbyint(bitsf(a) * 512.0f);  // exact scaling, RNE
+    return sign | (uint8_t)q;
+}
+
+static float host_e4m3_to_f32(uint8_t v)
+{
+    const uint32_t e = (v >> 3) & 15u, m = v & 7u;
+    float mag;
+    if (e == 15u && m == 7u) mag = NAN;
+    else if (e == 0u) mag = std::ldexp((float)m, -9);
+    else mag = bitsf(((e + 120u) << 23) | (m << 20));
+    return (v & 0x80u) ? -mag : mag;
+}
+
+}  // namespace mpk
+
+using namespace mpk;
+
+extern "C" {
+
+int mpk_version(void) { return 100; }
+
+const char* mpk_last_error(void) { return t_last_error; }
+
+const char* mpk_status_string(int status)
+{
+    switch (status) {
+    case MPK_SUCCESS: return "success";
+    case MPK_ERR_INVALID_VALUE: return "invalid value (null pointer or negative size)";
+    case MPK_ERR_UNSUPPORTED: return "unsupported shape (GEMM needs K % 16 == 0 and N % 8 == 0)";
+    case MPK_ERR_MISALIGNED: return "misaligned pointer (A_data and B must be 16-byte aligned)";
+    case MPK_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait expired";
+    case MPK_ERR_ARCH: return "current device is not sm_100";
+    case MPK_ERR_DRIVER: return "CUDA driver entry point or tensor-map encoding failed";
+    default: return status < 1000 ? cudaGetErrorString((cudaError_t)status) : "unknown status";
+    }
+}
+
+int mpk_set_wait_timeout_ns(uint64_t ns)
+{
+    if (ns == 0) {
+        set_last_error("wait timeout must be positive");
+        return MPK_ERR_INVALID_VALUE;
+    }
+    set_wait_timeout_ns(ns);
+    return MPK_SUCCESS;
+}
+
+int mpk_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
+                        const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
+                        uint8_t* D_scales, int M, int N, int K, void* stream)
+{
+    if (M < 0 || N < 0 || K < 0) {
+        set_last_error("negative size M=%d N=%d K=%d", M, N, K);
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (M == 0 || N == 0) return MPK_SUCCESS;
+    if (!D_data || !D_scales || (K > 0 && (!A_data || !A_scales || !B_bf16))) {
+        set_last_error("null device pointer");
+        return MPK_ERR_INVALID_VALUE;
+    }
+    // The reference adds C only when both C pointers are set
+    // (src/kernels/gemm_fp8_tensorcore.cu:188).
+    if (!C_data || !C_scales) C_data = nullptr, C_scales = nullptr;
+    if (int rc = check_arch()) return rc;
+    if (K == 0) {
+        // A*B is empty: D = MXFP8(C), or MXFP8(0) without C.
+        return from_cuda(launch_mxfp8_requantize(C_data, C_scales, D_data, D_scales, M, N,
+                                                 (cudaStream_t)stream),
+                         "requantize launch");
+    }
+    if (K % 16 != 0 || N % 8 != 0) {
+        set_last_error("GEMM needs K %% 16 == 0 and N %% 8 == 0 (TMA row strides); got N=%d K=%d", N, K);
+        return MPK_ERR_UNSUPPORTED;
+    }
+    if ((reinterpret_cast<uintptr_t>(A_data) & 15u) || (reinterpret_cast<uintptr_t>(B_bf16) & 15u)) {
+        set_last_error("A_data and B must be 16-byte aligned for TMA");
+        return MPK_ERR_MISALIGNED;
+    }
+    return launch_gemm_mxfp8_bf16(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales, M, N,
+                                  K, (cudaStream_t)stream);
+}
+
+int mpk_mxfp8_quantize(const float* input, uint8_t* data, uint8_t* scales, int M, int K, void* stream)
+{
+    if (M < 0 || K < 0) {
+        set_last_error("negative size M=%d K=%d", M, K);
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (M == 0 || K == 0) return MPK_SUCCESS;
+    if (!input || !data || !scales) {
+        set_last_error("null device pointer");
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (int rc = check_arch()) return rc;
+    return from_cuda(launch_mxfp8_quantize(input, data, scales, M, K, (cudaStream_t)stream),
+                     "quantize launch");
+}
+
+int mpk_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, float* output, int M, int K,
+                         void* stream)
+{
+    if (M < 0 || K < 0) {
+        set_last_error("negative size M=%d K=%d", M, K);
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (M == 0 || K == 0) return MPK_SUCCESS;
+    if (!data || !scales || !output) {
+        set_last_error("null device pointer");
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (int rc = check_arch()) return rc;
+    return from_cuda(launch_mxfp8_dequantize(data, scales, output, M, K, (cudaStream_t)stream),
+                     "dequantize launch");
+}
+
+int mpk_mxfp8_quantize_host(const float* input, uint8_t* data, uint8_t* scales, int M, int K)
+{
+    if (M < 0 || K < 0) return MPK_ERR_INVALID_VALUE;
+    if (M == 0 || K == 0) return MPK_SUCCESS;
+    if (!input || !data || !scales) return MPK_ERR_INVALID_VALUE;
+    const int64_t nblk = (K + 31) / 32;
+    for (int64_t r = 0; r < M; ++r) {
+        for (int64_t b = 0; b < nblk; ++b) {
+            const int64_t k0 = b * 32, k1 = (k0 + 32 < K) ? k0 + 32 : K;
+            const float* x = input + r * K;
+            float amax = 0.0f;
+            for (int64_t k = k0; k < k1; ++k) {
+                const float a = std::fabs(x[k]);
+                if (a > amax) amax = a;
+            }
+            float sv = amax / 448.0f;
+            if (sv < 1.1754944e-38f) sv = 1.1754944e-38f;
+            const uint8_t s = host_e8m0_roundup(sv);
+            const float actual = host_e8m0_to_f32(s);
+            const float inv = actual > 0.0f ? 1.0f / actual : 0.0f;
+            scales[r * nblk + b] = s;
+            for (int64_t k = k0; k < k1; ++k) data[r * K + k] = host_f32_to_e4m3(x[k] * inv);
+        }
+    }
+    return MPK_SUCCESS;
+}
+
+int mpk_mxfp8_dequantize_host(const uint8_t* data, const uint8_t* scales, float* output, int M, int K)
+{
+    if (M < 0 || K < 0) return MPK_ERR_INVALID_VALUE;
+    if (M == 0 || K == 0) return MPK_SUCCESS;
+    if (!data || !scales || !output) return MPK_ERR_INVALID_VALUE;
+    const int64_t nblk = (K + 31) / 32;
+    for (int64_t r = 0; r < M; ++r)
+        for (int64_t k = 0; k < K; ++k)
+            output[r * K + k] = host_e4m3_to_f32(data[r * K + k]) * host_e8m0_to_f32(scales[r * nblk + k / 32]);
+    return MPK_SUCCESS;
+}
+
+int mpk_device_status(int* device_status)
+{
+    int v = 0;
+    const int rc = read_and_clear_device_status(&v);
+    if (device_status) *device_status = v;
+    if (rc == MPK_ERR_DEVICE_TIMEOUT) set_last_error("device wait expired at site 0x%x", v);
+    return rc;
+}
+
+int mpk_wait_selftest(uint64_t timeout_ns, void* stream)
+{
+    if (int rc = check_arch()) return rc;
+    return launch_wait_selftest(timeout_ns, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,194 @@
+// MXFP8 quantize / dequantize as HBM-bandwidth kernels (sm_100a).
+//
+// Format (reference include/mxfp8_utils.h:24-47, src/quantize/*.cu):
+//   data   u8 [M][K] row-major, E4M3 codes
+//   scales u8 [M][ceil(K/32)] row-major, E8M0 bytes, one per 32 elements along K
+//
+// Both directions are bit-exact against the reference's host functions.
+//
+// Fast path (K % 32 == 0, 16-byte aligned pointers): the tensor is a flat run of
+// 32-element blocks whose scale index equals the flat block index, so a warp
+// streams 1 KiB of FP32 (quantize) or 256 B of codes (dequantize) per step with
+// fully coalesced 16-byte accesses.  Four lanes own one block (8 elements each);
+// the block amax is a two-step xor shuffle.  General path (ragged K, e.g.
+// K = 100, or unaligned pointers): one warp per (row, block), one element per lane.
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "mpk_ptx.cuh"
+#include "mpk_internal.h"
+
+namespace mpk {
+
+constexpr int kCodecThreads = 256;
+
+// ------------------------------- quantize ----------------------------------
+
+__global__ void __launch_bounds__(kCodecThreads)
+mxfp8_quantize_flat_kernel(const float* __restrict__ in, uint8_t* __restrict__ data,
+                           uint8_t* __restrict__ scales, int64_t n_quarters)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    // The trip count is warp-uniform (q - lane is the same for the whole warp and
+    // the stride is a multiple of 32), so the full-mask shuffles below are legal;
+    // lanes past the end compute on zeros and store nothing.
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q - lane < n_quarters;
+         q += stride) {
+        const bool valid = q < n_quarters;
+        float v[8];
+        if (valid) {
+            const float4* p = reinterpret_cast<const float4*>(in) + 2 * q;
+            float4 a = __ldcs(p), b = __ldcs(p + 1);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+            v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));  // NaN ignored
+        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+        float inv;
+        const uint32_t s = mx_block_scale(amax, inv);
+        if (valid) {
+            __stcs(reinterpret_cast<uint2*>(data) + q, quantize8(v, inv));
+            if ((q & 3) == 0) scales[q >> 2] = (uint8_t)s;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kCodecThreads)
+mxfp8_quantize_rowblock_kernel(const float* __restrict__ in, uint8_t* __restrict__ data,
+                               uint8_t* __restrict__ scales, int64_t M, int64_t K, int64_t nblk)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < M * nblk; w += warps) {
+        const int64_t row = w / nblk, blk = w % nblk;
+        const int64_t k = blk * 32 + lane;
+        const bool valid = k < K;
+        const float x = valid ? in[row * K + k] : 0.0f;
+        float amax = fmaxf(0.0f, fabsf(x));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+        float inv;
+        const uint32_t s = mx_block_scale(amax, inv);
+        if (valid) data[row * K + k] = (uint8_t)(f32x2_to_e4m3x2(x * inv, 0.0f) & 0xFFu);
+        if (lane == 0) scales[row * nblk + blk] = (uint8_t)s;
+    }
+}
+
+// D = MXFP8(C) (or MXFP8(0) without C): the K == 0 case of the GEMM, where the
+// product term is empty.  One warp per (row, block).
+__global__ void __launch_bounds__(kCodecThreads)
+mxfp8_requantize_kernel(const uint8_t* __restrict__ c_data, const uint8_t* __restrict__ c_scales,
+                        uint8_t* __restrict__ d_data, uint8_t* __restrict__ d_scales, int64_t M,
+                        int64_t N, int64_t nblk)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < M * nblk; w += warps) {
+        const int64_t row = w / nblk, blk = w % nblk;
+        const int64_t k = blk * 32 + lane;
+        const bool valid = k < N;
+        float x = 0.0f;
+        if (valid && c_data)
+            x = e4m3x2_to_f32x2(c_data[row * N + k]).x * e8m0_to_f32(c_scales[row * nblk + blk]);
+        float amax = fmaxf(0.0f, fabsf(x));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+        float inv;
+        const uint32_t s = mx_block_scale(amax, inv);
+        if (valid) d_data[row * N + k] = (uint8_t)(f32x2_to_e4m3x2(x * inv, 0.0f) & 0xFFu);
+        if (lane == 0) d_scales[row * nblk + blk] = (uint8_t)s;
+    }
+}
+
+// ------------------------------ dequantize ---------------------------------
+
+__global__ void __launch_bounds__(kCodecThreads)
+mxfp8_dequantize_flat_kernel(const uint8_t* __restrict__ data, const uint8_t* __restrict__ scales,
+                             float* __restrict__ out, int64_t n_octets)
+{
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < n_octets; o += stride) {
+        const uint2 c = __ldcs(reinterpret_cast<const uint2*>(data) + o);
+        const float s = e8m0_to_f32(__ldg(scales + (o >> 2)));
+        float2 f0 = e4m3x2_to_f32x2(c.x), f1 = e4m3x2_to_f32x2(c.x >> 16);
+        float2 f2 = e4m3x2_to_f32x2(c.y), f3 = e4m3x2_to_f32x2(c.y >> 16);
+        float4* p = reinterpret_cast<float4*>(out) + 2 * o;
+        __stcs(p, make_float4(f0.x * s, f0.y * s, f1.x * s, f1.y * s));
+        __stcs(p + 1, make_float4(f2.x * s, f2.y * s, f3.x * s, f3.y * s));
+    }
+}
+
+__global__ void __launch_bounds__(kCodecThreads)
+mxfp8_dequantize_elem_kernel(const uint8_t* __restrict__ data, const uint8_t* __restrict__ scales,
+                             float* __restrict__ out, int64_t M, int64_t K, int64_t nblk)
+{
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M * K; i += stride) {
+        const int64_t row = i / K, k = i % K;
+        const float s = e8m0_to_f32(scales[row * nblk + k / 32]);
+        out[i] = e4m3x2_to_f32x2(data[i]).x * s;
+    }
+}
+
+// ------------------------------- launchers ---------------------------------
+
+static int codec_grid(int64_t work_items)
+{
+    const int64_t per_block = kCodecThreads;
+    int64_t blocks = (work_items + per_block - 1) / per_block;
+    const int64_t cap = (int64_t)device_sm_count() * 8;  // 2048 threads per SM
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    return (int)blocks;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+cudaError_t launch_mxfp8_quantize(const float* in, uint8_t* data, uint8_t* scales, int64_t M,
+                                  int64_t K, cudaStream_t stream)
+{
+    const int64_t nblk = (K + 31) / 32;
+    if (M == 0 || K == 0) return cudaSuccess;
+    if (K % 32 == 0 && aligned16(in) && (reinterpret_cast<uintptr_t>(data) & 7u) == 0) {
+        const int64_t nq = M * K / 8;
+        mxfp8_quantize_flat_kernel<<<codec_grid(nq), kCodecThreads, 0, stream>>>(in, data, scales, nq);
+    } else {
+        mxfp8_quantize_rowblock_kernel<<<codec_grid(M * nblk * 32), kCodecThreads, 0, stream>>>(
+            in, data, scales, M, K, nblk);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, float* out,
+                                    int64_t M, int64_t K, cudaStream_t stream)
+{
+    const int64_t nblk = (K + 31) / 32;
+    if (M == 0 || K == 0) return cudaSuccess;
+    if (K % 32 == 0 && aligned16(out) && (reinterpret_cast<uintptr_t>(data) & 7u) == 0) {
+        const int64_t no = M * K / 8;
+        mxfp8_dequantize_flat_kernel<<<codec_grid(no), kCodecThreads, 0, stream>>>(data, scales, out, no);
+    } else {
+        mxfp8_dequantize_elem_kernel<<<codec_grid(M * K), kCodecThreads, 0, stream>>>(
+            data, scales, out, M, K, nblk);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mxfp8_requantize(const uint8_t* c_data, const uint8_t* c_scales, uint8_t* d_data,
+                                    uint8_t* d_scales, int64_t M, int64_t N, cudaStream_t stream)
+{
+    const int64_t nblk = (N + 31) / 32;
+    if (M == 0 || N == 0) return cudaSuccess;
+    mxfp8_requantize_kernel<<<codec_grid(M * nblk * 32), kCodecThreads, 0, stream>>>(
+        c_data, c_scales, d_data, d_scales, M, N, nblk);
+    return cudaGetLastError();
+}
+
+}  // namespace mpk

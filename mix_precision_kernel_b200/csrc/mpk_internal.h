@@ -1,0 +1,40 @@
+// Internal interfaces between the translation units of libmpk (not installed).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace mpk {
+
+// Device properties of the current device (cached per device).
+int device_sm_count();
+int device_cc_major();
+int device_cc_minor();
+
+// Codec launchers (codec.cu).  Arguments are validated by the ABI layer.
+cudaError_t launch_mxfp8_quantize(const float* in, uint8_t* data, uint8_t* scales, int64_t M,
+                                  int64_t K, cudaStream_t stream);
+cudaError_t launch_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, float* out,
+                                    int64_t M, int64_t K, cudaStream_t stream);
+// D = MXFP8(dequant(C)) along N (C may be null: D = MXFP8(0)).  The K == 0 GEMM.
+cudaError_t launch_mxfp8_requantize(const uint8_t* c_data, const uint8_t* c_scales, uint8_t* d_data,
+                                    uint8_t* d_scales, int64_t M, int64_t N, cudaStream_t stream);
+
+// GEMM launcher (gemm.cu).  Returns an MPK status code (0 on success).
+int launch_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const void* B,
+                           const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
+                           uint8_t* D_scales, int M, int N, int K, cudaStream_t stream);
+
+// Device-side status word of the GEMM kernels (gemm.cu): read and clear.
+int read_and_clear_device_status(int* value);
+// Bounded-wait self test: one CTA waits on an mbarrier that nothing arrives on.
+int launch_wait_selftest(uint64_t timeout_ns, cudaStream_t stream);
+
+// Wait budget for device-side spin waits, in nanoseconds.
+uint64_t wait_timeout_ns();
+void set_wait_timeout_ns(uint64_t ns);
+
+// Thread-local detail message for the last failing call.
+void set_last_error(const char* fmt, ...);
+
+}  // namespace mpk

@@ -1,0 +1,267 @@
+// Inline-PTX building blocks for sm_100a: mbarriers with bounded waits, TMA
+// tensor loads, tcgen05 (TMEM allocation, MMA, commit, loads) and the scalar
+// MXFP8 numerics shared by the codec and the GEMM epilogue.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace mpk {
+
+// ---------------------------------------------------------------------------
+// MXFP8 scalar numerics, device side.
+//
+// Semantics follow the reference's header-inline helpers:
+//   include/mxfp8_utils.h:8-11   e8m0 byte b -> float with bit pattern b<<23
+//                                (b=0 -> 0.0, b=255 -> +inf)
+//   include/mxfp8_utils.h:13-22  float -> e8m0, rounding up to a power of two
+//   include/fp8_types.h:8-12     E4M3 -> float, exact
+//   include/fp8_types.h:14-21    float -> E4M3: NaN -> 0x7F, clamp +-448, RNE
+// ---------------------------------------------------------------------------
+constexpr float kE4M3Max = 448.0f;
+constexpr float kScaleFloor = 1.1754944e-38f;  // src/quantize/mxfp8_quantize.cu:131
+
+__device__ __forceinline__ float e8m0_to_f32(uint32_t b) { return __uint_as_float(b << 23); }
+
+__device__ __forceinline__ uint32_t f32_to_e8m0_roundup(float x)
+{
+    if (x <= 0.0f) return 0u;
+    uint32_t bits = __float_as_uint(x);
+    uint32_t e = (bits >> 23) & 0xFFu;
+    if (bits & 0x007FFFFFu) e = (e < 255u) ? e + 1u : 255u;
+    return e;
+}
+
+// Two E4M3 codes (low byte = first element) -> two floats, exact.
+__device__ __forceinline__ float2 e4m3x2_to_f32x2(uint32_t two_codes)
+{
+    uint32_t h2;
+    asm("{\n\t.reg .b16 c;\n\tcvt.u16.u32 c, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, c;\n\t}"
+        : "=r"(h2) : "r"(two_codes));
+    float lo, hi;
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.f32.f16 %0, l;\n\tcvt.f32.f16 %1, h;\n\t}"
+        : "=f"(lo), "=f"(hi) : "r"(h2));
+    return make_float2(lo, hi);
+}
+
+// Clamp to +-448 and round to nearest even into E4M3; NaN -> 0x7F.
+// Returns two codes packed as (second << 8) | first.
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float first, float second)
+{
+    float a = fminf(fmaxf(first, -kE4M3Max), kE4M3Max);
+    float b = fminf(fmaxf(second, -kE4M3Max), kE4M3Max);
+    uint32_t r;
+    // cvt packs its first source into the upper byte.
+    asm("{\n\t.reg .b16 c;\n\tcvt.rn.satfinite.e4m3x2.f32 c, %1, %2;\n\tcvt.u32.u16 %0, c;\n\t}"
+        : "=r"(r) : "f"(b), "f"(a));
+    if (first != first) r = (r & 0xFF00u) | 0x7Fu;
+    if (second != second) r = (r & 0x00FFu) | 0x7F00u;
+    return r;
+}
+
+// Block scale for one MX block from its amax (src/quantize/mxfp8_quantize.cu:26-37):
+// returns the E8M0 byte and sets inv to 1/scale (0 when the scale is 0 or inf
+// maps to 0 through the division).
+__device__ __forceinline__ uint32_t mx_block_scale(float amax, float& inv)
+{
+    float scale_val = __fdiv_rn(amax, kE4M3Max);
+    if (scale_val < kScaleFloor) scale_val = kScaleFloor;
+    uint32_t s = f32_to_e8m0_roundup(scale_val);
+    float actual = e8m0_to_f32(s);
+    inv = (actual > 0.0f) ? __fdiv_rn(1.0f, actual) : 0.0f;
+    return s;
+}
+
+// Quantize 8 floats with a precomputed 1/scale; returns 8 codes little-endian.
+__device__ __forceinline__ uint2 quantize8(const float* v, float inv)
+{
+    uint32_t c0 = f32x2_to_e4m3x2(v[0] * inv, v[1] * inv);
+    uint32_t c1 = f32x2_to_e4m3x2(v[2] * inv, v[3] * inv);
+    uint32_t c2 = f32x2_to_e4m3x2(v[4] * inv, v[5] * inv);
+    uint32_t c3 = f32x2_to_e4m3x2(v[6] * inv, v[7] * inv);
+    return make_uint2(c0 | (c1 << 16), c2 | (c3 << 16));
+}
+
+// ---------------------------------------------------------------------------
+// Shared-memory addresses and mbarriers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar)
+{
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}"
+                 :: "r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;"
+                 :: "r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Error codes written to the device status word (see mpk.h MPK_ERR_DEVICE_TIMEOUT).
+constexpr int kDevTimeoutBase = 0x100;  // + wait site id
+
+// Bounded wait on an mbarrier phase.  Returns false (and raises the CTA's abort
+// flag and the device status word) if the phase does not complete within
+// timeout_ns, or if another warp of the CTA already aborted.  No wait in this
+// library can spin forever.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int* status, int site, uint64_t timeout_ns)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+#pragma unroll 1
+        for (int i = 0; i < 32; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > timeout_ns) {
+            *abort_flag = 1;
+            if (status) atomicCAS(status, 0, kDevTimeoutBase + site);
+            return false;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// TMA (tensor copies global -> shared, completion through an mbarrier)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint32_t bar,
+                                            int32_t x, int32_t y)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];"
+        :: "r"(dst), "l"(tmap), "r"(bar), "r"(x), "r"(y) : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const void* tmap)
+{
+    asm volatile("prefetch.tensormap [%0];" :: "l"(tmap) : "memory");
+}
+
+// Make generic-proxy shared-memory writes visible to the async proxy (tensor core).
+__device__ __forceinline__ void fence_proxy_async_smem()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05: tensor memory and the 5th-generation MMA
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t holder_smem, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(holder_smem), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish()
+{
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+                 :: "r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f16 (BF16 inputs, FP32 accumulate).
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                 :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+
+// Arrive on an mbarrier once all previously issued tcgen05.mma of this thread complete.
+__device__ __forceinline__ void umma_commit(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(bar) : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i of the warp receives row
+// (lane base + i), columns [col, col+32).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for tcgen05 (sm_100 layout):
+//   [0,14) start address >> 4, [16,30) leading byte offset >> 4,
+//   [32,46) stride byte offset >> 4, [46,48) version = 1,
+//   [49,52) base offset = 0, [52] LBO mode = 0, [61,64) layout (2 = 128-byte swizzle).
+__device__ __forceinline__ uint64_t umma_smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes,
+                                                         uint32_t sbo_bytes)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)2u << 61;
+    return d;
+}
+
+// Instruction descriptor for kind::f16: FP32 accumulator, BF16 A and B,
+// A K-major, B MN-major (the reference's B is [K][N] with N contiguous).
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int m, int n, bool b_mn_major)
+{
+    return (1u << 4)                         // D format: F32
+         | (1u << 7)                         // A format: BF16
+         | (1u << 10)                        // B format: BF16
+         | ((b_mn_major ? 1u : 0u) << 16)    // B major
+         | ((uint32_t)(n >> 3) << 17)        // N / 8
+         | ((uint32_t)(m >> 4) << 24);       // M / 16
+}
+
+}  // namespace mpk
