@@ -1,36 +1,39 @@
 // D = A*B + C with A in MXFP8, B in BF16 and C/D in MXFP8 (blocks along N):
-// a persistent, warp-specialised tcgen05 kernel for sm_100a.
+// a persistent, warp-specialised, 2-CTA tcgen05 kernel for sm_100a.
 //
 // Replaces the reference's launcher gemm_fp8_tensorcore
 // (src/kernels/gemm_fp8_tensorcore.cu:231-249), which runs a WMMA fp16 kernel
 // into an FP32 temporary it allocates per call, then quantizes that temporary in
 // a second kernel.  Here the whole path is one kernel and allocates nothing.
 //
-// Tile: 128 (M) x 256 (N) output per CTA, K stepped 64 at a time through a
-// 4-stage shared-memory ring.  Per stage:
-//   A codes  u8   128 x 64   8 KiB  TMA, 64-byte swizzle
-//   A bf16        128 x 64  16 KiB  written by the transform warps, K-major,
-//                                   128-byte swizzle (the UMMA canonical layout)
-//   B bf16         64 x 256 32 KiB  TMA, four 64x64 boxes, 128-byte swizzle,
-//                                   MN-major (B is [K][N] with N contiguous)
-//   A scales      128 x 2  loaded by the transform warps from global memory
+// Work decomposition.  Clusters of two CTAs on neighbouring SMs own 256 x 256
+// output tiles (persistent, tiles strided by the number of clusters, M fastest).
+// CTA rank r of the pair owns output rows [m0 + 128 r, +128) and loads only its
+// half of the tile's B columns, [n0 + 128 r, +128): the pair MMA
+// (tcgen05.mma.cta_group::2, M=256 N=256 K=16, issued by rank 0) reads A rows from
+// each CTA's own shared memory and B columns from both, and writes each CTA's
+// 128 x 256 FP32 accumulator into that CTA's tensor memory.  Versus one CTA per
+// 128 x 256 tile this halves the B bytes each SM pulls from L2 per MMA.
 //
-// Warp roles (10 warps):
-//   warp 0      TMA producer (A codes + B), one elected lane
-//   warp 1      TMEM owner and MMA issuer: tcgen05.mma.cta_group::1.kind::f16,
-//               M=128 N=256 K=16, FP32 accumulators in TMEM, two accumulator
-//               buffers of 256 columns so the epilogue of tile i overlaps the
-//               mainloop of tile i+1
-//   warps 2-5   transform: E4M3 code x 2^(scale-127) -> BF16, exact for scale
-//               bytes 3..246 (E4M3 has 4 significant bits and BF16 8), written
-//               in the swizzled K-major layout, then fence.proxy.async
-//   warps 6-9   epilogue: tcgen05.ld (one thread per accumulator row, 32
-//               consecutive columns = one MX block per load), + dequantized C,
-//               block amax, E8M0 scale, RNE E4M3, 16-byte stores
+// Per CTA and per K-step of 64 (STAGES-deep ring):
+//   A codes  u8   128 x 64   8 KiB  TMA (64-byte swizzle), completes on this CTA's full_a8
+//   A bf16        128 x 64  16 KiB  written by the transform warps, K-major, 128-byte
+//                                   swizzle (the UMMA canonical layout)
+//   B bf16         64 x 128 16 KiB  TMA, two 64x64 boxes, 128-byte swizzle, MN-major;
+//                                   completes on rank 0's full_b (.cta_group::2)
 //
-// Every mbarrier wait is bounded (mpk::mbar_wait); on expiry the CTA raises an
-// abort flag, records a status code, drains its in-flight TMA and MMA work with
-// a second bounded wait, frees TMEM and exits.
+// Warp roles (per CTA):
+//   warp 0   TMA producer (one lane)
+//   warp 1   TMEM owner (cta_group::2 allocation); on rank 0 also the MMA issuer
+//   warps 2+ transform: E4M3 code x 2^(scale-127) -> BF16 in shared memory (exact for
+//            scale bytes 3..246), then fence.proxy.async and an arrive on rank 0's
+//            full_a16 barrier
+//   last 4   epilogue: tcgen05.ld of this CTA's accumulator rows, + dequantized C,
+//            per-32-column amax, E8M0 scale, RNE E4M3, 16-byte stores
+//
+// Every mbarrier wait is bounded (mpk::mbar_wait*); on expiry the CTA raises an
+// abort flag, records a status code, drains the copies and MMAs it has in
+// flight with a second bounded wait, frees TMEM and exits.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -46,45 +49,60 @@
 namespace mpk {
 namespace gemm {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
+constexpr int BM = 128;        // rows per CTA; the pair covers 2*BM
+constexpr int PAIR_M = 2 * BM;
+constexpr int BN = 256;        // output columns per tile (each CTA loads BN/2 of B)
+constexpr int BN_HALF = BN / 2;
 constexpr int BK = 64;
-constexpr int STAGES = 4;
-constexpr int UMMA_K = 16;
-#ifndef MPK_TRANSFORM_WARPS
-#define MPK_TRANSFORM_WARPS 4
+#ifndef MPK_STAGES
+#define MPK_STAGES 5
 #endif
-constexpr int kTransformWarps = MPK_TRANSFORM_WARPS;  // 4 (one row per thread) or 8 (half rows)
-constexpr int kRowParts = kTransformWarps / 4;        // transform threads per tile row
-constexpr int kChunksPerThread = 4 / kRowParts;       // 16-element chunks per thread and stage
-static_assert(kTransformWarps == 4 || kTransformWarps == 8, "4 or 8 transform warps");
-constexpr int kEpilogueWarps = 4;
-// C chunks (32 columns each) the epilogue prefetches per round: the whole 256-column
-// row segment with 4 transform warps, half of it when registers are tighter.
-constexpr int kCPrefetch = kTransformWarps == 4 ? 8 : 4;
-constexpr int kThreads = 32 * (2 + kTransformWarps + kEpilogueWarps);
-constexpr int kFirstTransformWarp = 2;
-constexpr int kFirstEpilogueWarp = kFirstTransformWarp + kTransformWarps;
+constexpr int STAGES = MPK_STAGES;      // ring of B halves + BF16 A tiles (consumed by the MMA)
+#ifndef MPK_A8_STAGES
+#define MPK_A8_STAGES 8
+#endif
+constexpr int A8_STAGES = MPK_A8_STAGES;  // ring of A code tiles (consumed by the transform)
+constexpr int UMMA_K = 16;
 
-constexpr int A8_BYTES = BM * BK;           // 8192
-constexpr int A16_BYTES = BM * BK * 2;      // 16384
-constexpr int B_BOX_BYTES = 64 * BK * 2;    // one 64(N) x 64(K) box: 8192
-constexpr int B_BYTES = BK * BN * 2;        // 32768
-constexpr uint32_t kTxBytes = A8_BYTES + B_BYTES;
-constexpr uint32_t kTmemCols = 2 * BN;      // two FP32 accumulators
+#ifndef MPK_TRANSFORM_GROUPS
+#define MPK_TRANSFORM_GROUPS 2
+#endif
+// Transform warps come in groups of 4 (one thread per tile row).  Group g converts
+// the K-steps kb with kb % G == g, so G stages are in conversion at once and each
+// group's per-stage latencies (fence, arrive, waits) overlap the others' work.
+constexpr int kTransformGroups = MPK_TRANSFORM_GROUPS;
+static_assert(kTransformGroups == 1 || kTransformGroups == 2 || kTransformGroups == 4, "1, 2 or 4");
+constexpr int kTransformWarps = 4 * kTransformGroups;
+constexpr int kEpilogueWarps = 4;
+constexpr int kFirstTransformWarp = 3;
+constexpr int kFirstEpilogueWarp = kFirstTransformWarp + kTransformWarps;
+constexpr int kThreads = 32 * (kFirstEpilogueWarp + kEpilogueWarps);
+#ifndef MPK_C_PREFETCH
+#define MPK_C_PREFETCH (kTransformGroups <= 2 ? 4 : 2)
+#endif
+constexpr int kCPrefetch = MPK_C_PREFETCH;  // C chunks (32 columns) prefetched per round
+
+constexpr int A8_BYTES = BM * BK;               // 8192
+constexpr int A16_BYTES = BM * BK * 2;          // 16384
+constexpr int B_BOX_BYTES = 64 * BK * 2;        // one 64(N) x 64(K) box: 8192
+constexpr int B_BYTES = BK * BN_HALF * 2;       // 16384 per CTA
+constexpr uint32_t kTmemCols = 2 * BN;          // two FP32 accumulators of BN columns
 
 constexpr int OFF_B = 0;
 constexpr int OFF_A16 = OFF_B + STAGES * B_BYTES;
 constexpr int OFF_A8 = OFF_A16 + STAGES * A16_BYTES;
-constexpr int OFF_BAR = OFF_A8 + STAGES * A8_BYTES;
-// barriers: full_tma[S], full_a16[S], empty[S], tfull[2], tempty[2], drain
-constexpr int kNumBars = 3 * STAGES + 5;
+constexpr int OFF_BAR = OFF_A8 + A8_STAGES * A8_BYTES;
+// barriers: a8_full[S8], a8_empty[S8], full_b[S], full_a16[S], empty[S], tfull[2],
+// tempty[2], drain
+constexpr int kNumBars = 2 * A8_STAGES + 3 * STAGES + 5;
 constexpr int OFF_MISC = OFF_BAR + kNumBars * 8;
 constexpr int SMEM_USED = OFF_MISC + 16;
 constexpr int SMEM_BYTES = SMEM_USED + 1024;  // slack for 1024-byte alignment
 static_assert(SMEM_BYTES <= 232448, "exceeds the sm_100 per-block shared memory limit");
+static_assert(A8_STAGES >= STAGES, "the transform's phase waits assume A8_STAGES >= STAGES");
 
-constexpr uint32_t kIdesc = umma_idesc_bf16_f32(BM, BN, /*b_mn_major=*/true);
+// Pair MMA: M = 256 across the two CTAs, N = 256, B MN-major.
+constexpr uint32_t kIdesc = umma_idesc_bf16_f32(PAIR_M, BN, /*b_mn_major=*/true);
 constexpr uint64_t kDrainTimeoutNs = 200000000ull;  // teardown waits: 0.2 s
 
 struct Params {
@@ -102,11 +120,12 @@ struct Params {
 };
 
 // Wait-site ids reported in the device status word.
-enum { kSiteEmpty = 1, kSiteFullTma = 2, kSiteFullA16 = 3, kSiteTmemEmpty = 4, kSiteTmemFull = 5 };
+enum { kSiteEmpty = 1, kSiteFullB = 2, kSiteFullA16 = 3, kSiteTmemEmpty = 4, kSiteTmemFull = 5,
+       kSiteFullA8 = 6, kSiteEmptyA8 = 7, kSiteEmptyT = 8 };
 
 __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& m0, int& n0)
 {
-    m0 = (tile % p.num_m_tiles) * BM;  // M fastest: consecutive CTAs share a B column band
+    m0 = (tile % p.num_m_tiles) * PAIR_M;  // M fastest: consecutive clusters share a B column band
     n0 = (tile / p.num_m_tiles) * BN;
 }
 
@@ -127,25 +146,111 @@ __device__ __forceinline__ uint4 load_scale_group(const uint8_t* __restrict__ ro
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// 16 E4M3 codes with one E8M0 scale -> 16 BF16 (two 16-byte chunks), exact for
-// scale bytes 3..246: code * 2^(s-127) is formed exactly in FP32 and rounded to
-// BF16, where it is representable.
-__device__ __forceinline__ void transform16(const uint4 q, float scale, uint4& o0, uint4& o1)
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel)
 {
-    uint32_t out[8];
-    const uint32_t in[4] = {q.x, q.y, q.z, q.w};
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b)
+{
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// 16 E4M3 codes sharing one E8M0 scale byte s -> 16 BF16 (two 16-byte chunks).
+//
+// Fast path (scale bytes 3..134, no NaN code): each code's sign and 7 magnitude
+// bits are moved into a BF16 bit pattern equal to code x 2^-120 (the E4M3
+// exponent bits land in the low BF16 exponent bits; E4M3 subnormals become BF16
+// subnormals), then one BF16 multiply by 2^(s-7) -- a power of two, so exact --
+// gives code x 2^(s-127).  Integer ops and mul.rn.bf16x2 only.
+// Slow path (any scale, NaN codes): E4M3 -> f16 -> f32 with hardware conversions,
+// multiply by the FP32 scale (0 -> 0.0, 255 -> inf as in the reference), round to
+// BF16.  Both paths are exact wherever the product is representable in BF16
+// (scale bytes 3..246).
+// One row of one K-step: 64 E4M3 codes (four 16-code chunks) with the
+// E8M0 scale bytes s0 (codes 0..31) and s1 (codes 32..63) -> 64 BF16 written as
+// eight 16-byte chunks into the 128B-swizzled row at `row` (chunk c lands at
+// ((c ^ xr) << 4)).  Chunks at K offset >= kvalid are written as zeros.
+//
+// Exact general path: E4M3 -> f16 -> f32 with hardware conversions, multiply by
+// the FP32 scale (byte 0 -> 0.0 and 255 -> inf, as in the reference), round to
+// BF16.  Used for scale bytes outside 3..134, NaN codes and the K tail; kept out of
+// line so the hot loop stays small.
+__device__ __noinline__ void transform_row_exact(const uint8_t* a8row, uint32_t a8xr, uint32_t s0,
+                                                 uint32_t s1, uint8_t* row, uint32_t xr, int kvalid)
+{
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+        uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+        if (16 * c < kvalid) {
+            // The codes are re-read from the A-code tile (64-byte swizzled row).
+            const uint4 qc = *reinterpret_cast<const uint4*>(a8row + ((((uint32_t)c) ^ a8xr) << 4));
+            const uint32_t in[4] = {qc.x, qc.y, qc.z, qc.w};
+            const float scale = e8m0_to_f32(c < 2 ? s0 : s1);
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
+            for (int w = 0; w < 4; ++w) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const float2 f = e4m3x2_to_f32x2(in[w] >> (16 * h));
-            uint32_t packed;
-            asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed) : "f"(f.y * scale), "f"(f.x * scale));
-            out[2 * w + h] = packed;
+                for (int h = 0; h < 2; ++h) {
+                    const float2 f = e4m3x2_to_f32x2(in[w] >> (16 * h));
+                    uint32_t packed;
+                    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed) : "f"(f.y * scale), "f"(f.x * scale));
+                    out[2 * w + h] = packed;
+                }
+            }
+        }
+        *reinterpret_cast<uint4*>(row + ((((uint32_t)(2 * c)) ^ xr) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
+        *reinterpret_cast<uint4*>(row + ((((uint32_t)(2 * c + 1)) ^ xr) << 4)) = make_uint4(out[4], out[5], out[6], out[7]);
+    }
+}
+
+// Fast path for one row of one K-step (same contract as transform_row_exact, with
+// the four code chunks already loaded into q[0..3]),
+// valid when both scale bytes are in 3..134, no code is NaN (0x7F/0xFF) and all 64
+// codes are inside K.  Each code's sign and 7 magnitude bits are moved into a BF16
+// bit pattern equal to code x 2^-120 (the E4M3 exponent bits land in the low BF16
+// exponent bits; E4M3 subnormals become BF16 subnormals); one BF16 multiply by
+// 2^(s-7) -- a power of two, so exact -- gives code x 2^(s-127).  Integer ops and
+// mul.rn.bf16x2 only, straight-line over the four chunks.  Returns false (writing
+// nothing) when the preconditions do not hold.
+__device__ __forceinline__ bool transform_row_fast(const uint4* q, uint32_t s0, uint32_t s1, uint8_t* row,
+                                                   uint32_t xr, int kvalid)
+{
+    uint32_t wm[16], nan_probe = 0u;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint32_t in[4] = {q[c].x, q[c].y, q[c].z, q[c].w};
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            wm[4 * c + w] = in[w] & 0x7F7F7F7Fu;
+            nan_probe |= wm[4 * c + w] + 0x01010101u;  // a byte 0x7F becomes 0x80
         }
     }
-    o0 = make_uint4(out[0], out[1], out[2], out[3]);
-    o1 = make_uint4(out[4], out[5], out[6], out[7]);
+    if ((s0 - 3u) > 131u || (s1 - 3u) > 131u || (nan_probe & 0x80808080u) != 0u || kvalid < 64)
+        return false;
+    uint32_t f0 = (s0 + 120u) << 7, f1 = (s1 + 120u) << 7;  // BF16 2^(s-7)
+    f0 |= f0 << 16;
+    f1 |= f1 << 16;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint32_t in[4] = {q[c].x, q[c].y, q[c].z, q[c].w};
+        const uint32_t f = c < 2 ? f0 : f1;
+        uint32_t out[8];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const uint32_t ws = in[w] & 0x80808080u;
+            const uint32_t m01 = prmt(wm[4 * c + w], 0u, 0x4140u), s01 = prmt(ws, 0u, 0x1404u);
+            const uint32_t m23 = prmt(wm[4 * c + w], 0u, 0x4342u), s23 = prmt(ws, 0u, 0x3424u);
+            out[2 * w] = mul_bf16x2(m01 * 16u + s01, f);
+            out[2 * w + 1] = mul_bf16x2(m23 * 16u + s23, f);
+        }
+        *reinterpret_cast<uint4*>(row + ((((uint32_t)(2 * c)) ^ xr) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
+        *reinterpret_cast<uint4*>(row + ((((uint32_t)(2 * c + 1)) ^ xr) << 4)) = make_uint4(out[4], out[5], out[6], out[7]);
+    }
+    return true;
 }
 
 // Epilogue math for one MX block of 32 accumulator values of one row.
@@ -163,22 +268,56 @@ __device__ __forceinline__ uint32_t quantize_block32(float (&v)[32], uint4& c0, 
     return s;
 }
 
+// Ragged or unaligned 32-column chunk of one accumulator row: loads the chunk
+// from TMEM itself (warp-collective; every lane calls this together), element-wise
+// C loads and D stores, columns past N kept out of the block amax.  Out of line to
+// keep the epilogue's hot code small.
+__device__ __noinline__ void epilogue_ragged_chunk(const Params& p, uint32_t taddr, uint32_t cscale,
+                                                   bool has_c, bool row_ok, int64_t grow, int col0,
+                                                   int valid)
+{
+    uint32_t raw[32];
+    tmem_ld_32x32b_x32(taddr, raw);
+    tmem_ld_wait();
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = (i < valid) ? __uint_as_float(raw[i]) : 0.0f;
+    if (has_c && row_ok) {
+        const float sc = e8m0_to_f32(cscale);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (i < valid) v[i] += e4m3x2_to_f32x2(p.C_data[grow * p.N + col0 + i]).x * sc;
+    }
+    uint4 d0, d1;
+    const uint32_t sd = quantize_block32(v, d0, d1);
+    if (row_ok) {
+        const uint32_t dw[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (i < valid) p.D_data[grow * p.N + col0 + i] = (uint8_t)(dw[i >> 2] >> (8 * (i & 3)));
+        p.D_scales[grow * p.nblkN + col0 / 32] = (uint8_t)sd;
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                        const __grid_constant__ CUtensorMap tmap_b, const Params p)
 {
     extern __shared__ uint8_t smem_raw[];
     // Swizzled TMA destinations and UMMA descriptors need 1024-byte alignment of
-    // the shared-memory address itself.
+    // the shared-memory address itself; both CTAs of the pair get the same offsets.
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar0 = sbase + OFF_BAR;
-    auto full_tma = [&](int s) { return bar0 + 8u * s; };
-    auto full_a16 = [&](int s) { return bar0 + 8u * (STAGES + s); };
-    auto empty = [&](int s) { return bar0 + 8u * (2 * STAGES + s); };
-    auto tfull = [&](int a) { return bar0 + 8u * (3 * STAGES + a); };
-    auto tempty = [&](int a) { return bar0 + 8u * (3 * STAGES + 2 + a); };
-    const uint32_t drain = bar0 + 8u * (3 * STAGES + 4);
+    auto a8_full = [&](int j) { return bar0 + 8u * j; };
+    auto a8_empty = [&](int j) { return bar0 + 8u * (A8_STAGES + j); };
+    const uint32_t barS = bar0 + 8u * (2 * A8_STAGES);
+    auto full_b = [&](int s) { return barS + 8u * s; };
+    auto full_a16 = [&](int s) { return barS + 8u * (STAGES + s); };
+    auto empty = [&](int s) { return barS + 8u * (2 * STAGES + s); };
+    auto tfull = [&](int a) { return barS + 8u * (3 * STAGES + a); };
+    auto tempty = [&](int a) { return barS + 8u * (3 * STAGES + 2 + a); };
+    const uint32_t drain = barS + 8u * (3 * STAGES + 4);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
     // Stays 0: the abort flag of the teardown waits, which must not be cut short.
@@ -186,17 +325,24 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();     // 0 = MMA leader of the pair
+    const int cluster = (int)cluster_id_x();
+    const int nclusters = (int)nclusters_x();
     const int num_tiles = p.num_m_tiles * p.num_n_tiles;
 
     if (threadIdx.x == 0) {
+        for (int j = 0; j < A8_STAGES; ++j) {
+            mbar_init(a8_full(j), 1);
+            mbar_init(a8_empty(j), 4);  // the 4 warps of the transform group that read it
+        }
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(full_tma(s), 1);
-            mbar_init(full_a16(s), kTransformWarps);
+            mbar_init(full_b(s), 1);
+            mbar_init(full_a16(s), 2 * 4);  // one transform group per stage, both CTAs
             mbar_init(empty(s), 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull(a), 1);
-            mbar_init(tempty(a), kEpilogueWarps);
+            mbar_init(tempty(a), 2 * kEpilogueWarps);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -204,62 +350,97 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_holder), kTmemCols);
-        tmem_relinquish();
+        tmem_alloc_pair(smem_u32(tmem_holder), kTmemCols);
+        tmem_relinquish_pair();
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated in both
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
+    bool producer_aborted = false;
 
     if (warp == 0) {
-        // ------------------------------ TMA producer ------------------------------
+        // ---------------------------- B producer (TMA) ----------------------------
         if (lane == 0) {
-            prefetch_tmap(&tmap_a);
             prefetch_tmap(&tmap_b);
             int s = 0;
             uint32_t ph = 0;
             int issued = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+            for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
                 int m0, n0;
                 tile_coords(p, tile, m0, n0);
+                const int col0 = n0 + BN_HALF * (int)rank;
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, p.status, kSiteEmpty, p.timeout_ns)) {
                         ok = false;
                         break;
                     }
-                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
-                                 :: "r"(full_tma(s)), "r"(kTxBytes) : "memory");
-                    const int k0 = kb * BK;
-                    tma_load_2d(sbase + OFF_A8 + s * A8_BYTES, &tmap_a, full_tma(s), k0, m0);
+                    // B halves of both CTAs complete on rank 0's full_b.
+                    if (rank == 0) mbar_arrive_expect_tx(full_b(s), 2 * B_BYTES);
+                    const uint32_t fb = mapa_shared(full_b(s), 0);
 #pragma unroll
-                    for (int j = 0; j < BN / 64; ++j)
-                        tma_load_2d(sbase + OFF_B + s * B_BYTES + j * B_BOX_BYTES, &tmap_b, full_tma(s),
-                                    n0 + 64 * j, k0);
+                    for (int j = 0; j < BN_HALF / 64; ++j)
+                        tma_load_2d_pair(sbase + OFF_B + s * B_BYTES + j * B_BOX_BYTES, &tmap_b, fb,
+                                         col0 + 64 * j, kb * BK);
                     ++issued;
                     if (++s == STAGES) { s = 0; ph ^= 1u; }
                 }
             }
             if (!ok) {
+                producer_aborted = true;
                 // Let the copies already issued land before the CTA can exit.
                 const int outstanding = issued < STAGES ? issued : STAGES;
                 int ss = s;
                 uint32_t pp = ph;
                 for (int i = 0; i < outstanding; ++i) {
                     if (--ss < 0) { ss = STAGES - 1; pp ^= 1u; }
-                    mbar_wait(full_tma(ss), pp, never_abort, nullptr, 0, kDrainTimeoutNs);
+                    if (rank == 0) mbar_wait(full_b(ss), pp, never_abort, nullptr, 0, kDrainTimeoutNs);
+                }
+            }
+        }
+    } else if (warp == 2) {
+        // -------------------------- A-code producer (TMA) --------------------------
+        if (lane == 0) {
+            prefetch_tmap(&tmap_a);
+            int j = 0;
+            uint32_t ph = 0;
+            int issued = 0;
+            bool ok = true;
+            for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
+                int m0, n0;
+                tile_coords(p, tile, m0, n0);
+                const int row0 = m0 + BM * (int)rank;
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(a8_empty(j), ph ^ 1u, abort_flag, p.status, kSiteEmptyA8, p.timeout_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(a8_full(j), A8_BYTES);
+                    tma_load_2d(sbase + OFF_A8 + j * A8_BYTES, &tmap_a, a8_full(j), kb * BK, row0);
+                    ++issued;
+                    if (++j == A8_STAGES) { j = 0; ph ^= 1u; }
+                }
+            }
+            if (!ok) {
+                producer_aborted = true;
+                const int outstanding = issued < A8_STAGES ? issued : A8_STAGES;
+                int jj = j;
+                uint32_t pp = ph;
+                for (int i = 0; i < outstanding; ++i) {
+                    if (--jj < 0) { jj = A8_STAGES - 1; pp ^= 1u; }
+                    mbar_wait(a8_full(jj), pp, never_abort, nullptr, 0, kDrainTimeoutNs);
                 }
             }
         }
     } else if (warp == 1) {
-        // ------------------------------- MMA issuer -------------------------------
-        if (lane == 0) {
+        // --------------------------- MMA issuer (rank 0) ---------------------------
+        if (rank == 0 && lane == 0) {
             int s = 0;
             uint32_t ph = 0;
             int it = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++it) {
+            for (int tile = cluster; ok && tile < num_tiles; tile += nclusters, ++it) {
                 const int acc = it & 1;
                 const uint32_t acc_ph = (uint32_t)(it >> 1) & 1u;
                 if (!mbar_wait(tempty(acc), acc_ph ^ 1u, abort_flag, p.status, kSiteTmemEmpty,
@@ -270,7 +451,7 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
-                    if (!mbar_wait(full_tma(s), ph, abort_flag, p.status, kSiteFullTma, p.timeout_ns) ||
+                    if (!mbar_wait(full_b(s), ph, abort_flag, p.status, kSiteFullB, p.timeout_ns) ||
                         !mbar_wait(full_a16(s), ph, abort_flag, p.status, kSiteFullA16, p.timeout_ns)) {
                         ok = false;
                         break;
@@ -286,98 +467,107 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                         // B: MN-major, 64-column chunks 8 KiB apart (LBO), 8-row K groups
                         // 1024 B apart (SBO); a K step of 16 rows is 2 KiB.
                         const uint64_t bdesc = umma_smem_desc_sw128(b_addr + k * UMMA_K * 128, B_BOX_BYTES, 1024);
-                        umma_bf16(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0 ? 1u : 0u);
+                        umma_bf16_pair(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0 ? 1u : 0u);
                     }
-                    umma_commit(empty(s));
+                    umma_commit_pair_mc(empty(s), 0x3);  // frees slot s in both CTAs
                     if (++s == STAGES) { s = 0; ph ^= 1u; }
                 }
                 if (!ok) break;
-                umma_commit(tfull(acc));
+                umma_commit_pair_mc(tfull(acc), 0x3);
             }
-            // All MMAs issued by this thread complete before TMEM is released.
-            umma_commit(drain);
+            // All pair MMAs issued by this thread complete before TMEM is released.
+            umma_commit_pair(drain);
             mbar_wait(drain, 0, never_abort, nullptr, 0, kDrainTimeoutNs);
         }
     } else if (warp < kFirstEpilogueWarp) {
         // ------------------------------- transform --------------------------------
-        // Thread t owns tile row r = t % 128 and, with 8 transform warps, half of its
-        // 64 K-elements per stage (one MX block).  A warp covers 32 consecutive rows,
-        // which keeps the 64B-swizzled reads and 128B-swizzled writes conflict-free.
+        // Group g (4 warps, one thread per row of this CTA's A tile) converts the
+        // K-steps kb with kb % G == g.  A warp covers 32 consecutive rows, which keeps
+        // the 64B-swizzled reads and the 128B-swizzled writes conflict-free.
         const int t = threadIdx.x - 32 * kFirstTransformWarp;
         const int r = t & (BM - 1);
-        const int part = t / BM;
-        const int groups = (p.num_kb + 7) / 8;                 // 8 k-steps per scale group
-        int s = 0;
-        uint32_t ph = 0;
+        const int grp = t / BM;
+        const int groups = (p.num_kb + 7) / 8;  // 8 k-steps per scale group
+        const uint32_t fa16_base = mapa_shared(full_a16(0), 0);
         bool ok = true;
-        int tile = blockIdx.x;
+        int tile = cluster;
         int m0 = 0, n0 = 0;
         if (tile < num_tiles) tile_coords(p, tile, m0, n0);
-        uint4 nxt = load_scale_group(p.A_scales + (int64_t)(m0 + r) * p.nblkK, 0, p.nblkK,
-                                     tile < num_tiles && m0 + r < p.M);
+        int grow = m0 + BM * (int)rank + r;
+        uint4 nxt = load_scale_group(p.A_scales + (int64_t)grow * p.nblkK, 0, p.nblkK,
+                                     tile < num_tiles && grow < p.M);
         const uint32_t a8_row_off = (uint32_t)r * 64u;
         const uint32_t a8_xor = (uint32_t)((r >> 1) & 3);
         const uint32_t a16_row_off = (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
         const uint32_t a16_xor = (uint32_t)(r & 7);
-        for (; ok && tile < num_tiles; tile += gridDim.x) {
+        int64_t base_stage = 0;  // global stage index of kb = 0 of the current tile
+        for (; ok && tile < num_tiles; tile += nclusters, base_stage += p.num_kb) {
             tile_coords(p, tile, m0, n0);
             for (int g = 0; ok && g < groups; ++g) {
                 const uint4 cur = nxt;
                 {   // prefetch the next scale group (same tile, or the first of the next tile)
                     int nt = tile, ng = g + 1;
-                    if (ng == groups) { nt = tile + gridDim.x; ng = 0; }
+                    if (ng == groups) { nt = tile + nclusters; ng = 0; }
                     int nm0 = m0, nn0;
                     if (nt < num_tiles) tile_coords(p, nt, nm0, nn0);
-                    nxt = load_scale_group(p.A_scales + (int64_t)(nm0 + r) * p.nblkK, 16 * ng, p.nblkK,
-                                           nt < num_tiles && nm0 + r < p.M);
+                    const int nrow = nm0 + BM * (int)rank + r;
+                    nxt = load_scale_group(p.A_scales + (int64_t)nrow * p.nblkK, 16 * ng, p.nblkK,
+                                           nt < num_tiles && nrow < p.M);
                 }
-                const uint32_t cw[4] = {cur.x, cur.y, cur.z, cur.w};
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
+                const uint64_t sc_lo = ((uint64_t)cur.y << 32) | cur.x;  // k-steps 0..3 of the group
+                const uint64_t sc_hi = ((uint64_t)cur.w << 32) | cur.z;  // k-steps 4..7
+#pragma unroll 1
+                for (int j = grp; j < 8; j += kTransformGroups) {
                     const int kb = g * 8 + j;
                     if (kb >= p.num_kb) break;
-                    if (!mbar_wait(full_tma(s), ph, abort_flag, p.status, kSiteFullTma, p.timeout_ns)) {
+                    const int64_t i = base_stage + kb;  // global stage index
+                    const int s = (int)(i % STAGES);
+                    const uint32_t ph = (uint32_t)((i / STAGES) & 1);
+                    const int j8 = (int)(i % A8_STAGES);
+                    const uint32_t ph8 = (uint32_t)((i / A8_STAGES) & 1);
+                    // The BF16 slot is free once the MMAs of its previous round completed.
+                    // Waiting on it first also keeps every group within STAGES (<=
+                    // A8_STAGES) stages of the MMA, so no parity wait below can match a
+                    // phase one round too old.
+                    if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, p.status, kSiteEmptyT, p.timeout_ns) ||
+                        !mbar_wait(a8_full(j8), ph8, abort_flag, p.status, kSiteFullA8, p.timeout_ns)) {
                         ok = false;
                         break;
                     }
-                    const uint8_t* a8 = smem + OFF_A8 + s * A8_BYTES;
-                    uint8_t* a16 = smem + OFF_A16 + s * A16_BYTES;
-                    const uint32_t sc2 = (cw[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;
-                    uint4 q[kChunksPerThread];
+                    const uint8_t* a8 = smem + OFF_A8 + j8 * A8_BYTES;
+                    uint4 q[4];
 #pragma unroll
-                    for (int cc = 0; cc < kChunksPerThread; ++cc) {
-                        const uint32_t c = (uint32_t)(part * kChunksPerThread + cc);
-                        q[cc] = *reinterpret_cast<const uint4*>(a8 + a8_row_off + ((c ^ a8_xor) << 4));
-                    }
-#pragma unroll
-                    for (int cc = 0; cc < kChunksPerThread; ++cc) {
-                        const uint32_t c = (uint32_t)(part * kChunksPerThread + cc);
-                        uint4 o0 = make_uint4(0u, 0u, 0u, 0u), o1 = o0;
-                        if (kb * BK + 16 * (int)c < p.K)  // K % 16 == 0: chunks are all in or all out
-                            transform16(q[cc], e8m0_to_f32((sc2 >> (8 * (c >> 1))) & 0xFFu), o0, o1);
-                        *reinterpret_cast<uint4*>(a16 + a16_row_off + (((2 * c) ^ a16_xor) << 4)) = o0;
-                        *reinterpret_cast<uint4*>(a16 + a16_row_off + (((2 * c + 1) ^ a16_xor) << 4)) = o1;
-                    }
+                    for (int c = 0; c < 4; ++c)
+                        q[c] = *reinterpret_cast<const uint4*>(a8 + a8_row_off + ((((uint32_t)c) ^ a8_xor) << 4));
+                    const uint32_t sc2 = (uint32_t)(((j < 4) ? sc_lo : sc_hi) >> (16 * (j & 3))) & 0xFFFFu;
+                    uint8_t* a16 = smem + OFF_A16 + s * A16_BYTES + a16_row_off;
+                    const uint32_t s0 = sc2 & 0xFFu, s1 = sc2 >> 8;
+                    const int kvalid = p.K - kb * BK;
+                    if (!transform_row_fast(q, s0, s1, a16, a16_xor, kvalid))
+                        transform_row_exact(a8 + a8_row_off, a8_xor, s0, s1, a16, a16_xor, kvalid);
+                    // The codes are consumed: release the A-code slot to the producer.
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(a8_empty(j8));
                     fence_proxy_async_smem();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(full_a16(s));
-                    if (++s == STAGES) { s = 0; ph ^= 1u; }
+                    if (lane == 0) mbar_arrive_cluster(fa16_base + 8u * s);
                 }
             }
         }
     } else {
         // -------------------------------- epilogue --------------------------------
         const int quad = warp & 3;                 // TMEM lanes this warp may access
-        const int r = quad * 32 + lane;            // accumulator row within the tile
+        const int r = quad * 32 + lane;            // accumulator row within this CTA's tile
         const bool has_c = p.C_data != nullptr;
+        const uint32_t tempty_base = mapa_shared(tempty(0), 0);
         bool aborted = false;
         int it = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+        for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
             int m0, n0;
             tile_coords(p, tile, m0, n0);
             const int acc = it & 1;
             const uint32_t acc_ph = (uint32_t)(it >> 1) & 1u;
-            const int64_t grow = (int64_t)m0 + r;
+            const int64_t grow = (int64_t)m0 + BM * (int)rank + r;
             const bool row_ok = grow < p.M;
             const int nchunks = min(BN / 32, (p.N - n0 + 31) / 32);
             bool full_seen = false;
@@ -415,15 +605,16 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 for (int ci = 0; ci < kCPrefetch; ++ci) {
                     const int c = c0 + ci;
                     if (c >= nchunks) break;  // warp-uniform: tcgen05.ld is warp-collective
-                    uint32_t raw[32];
-                    tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + 32 * c), raw);
-                    tmem_ld_wait();
-                    float v[32];
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]);
                     const int col0 = n0 + 32 * c;
                     const int valid = min(32, p.N - col0);
+                    const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + 32 * c);
                     if (valid == 32 && p.vec_cd) {
+                        uint32_t raw[32];
+                        tmem_ld_32x32b_x32(taddr, raw);
+                        tmem_ld_wait();
+                        float v[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]);
                         if (has_c) {
                             const float sc = e8m0_to_f32(cs[ci]);
                             const uint32_t cw[8] = {cq[ci][0].x, cq[ci][0].y, cq[ci][0].z, cq[ci][0].w,
@@ -447,42 +638,31 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                             p.D_scales[grow * p.nblkN + col0 / 32] = (uint8_t)sd;
                         }
                     } else {
-                        // Ragged or unaligned chunk: element-wise C loads and D stores.
-                        if (has_c && row_ok) {
-                            const float sc = e8m0_to_f32(cs[ci]);
-#pragma unroll
-                            for (int i = 0; i < 32; ++i)
-                                if (i < valid)
-                                    v[i] += e4m3x2_to_f32x2(p.C_data[grow * p.N + col0 + i]).x * sc;
-                        }
-#pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (i >= valid) v[i] = 0.0f;  // columns past N do not enter the amax
-                        uint4 d0, d1;
-                        const uint32_t sd = quantize_block32(v, d0, d1);
-                        if (row_ok) {
-                            const uint32_t dw[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
-#pragma unroll
-                            for (int i = 0; i < 32; ++i)
-                                if (i < valid) p.D_data[grow * p.N + col0 + i] = (uint8_t)(dw[i >> 2] >> (8 * (i & 3)));
-                            p.D_scales[grow * p.nblkN + col0 / 32] = (uint8_t)sd;
-                        }
+                        epilogue_ragged_chunk(p, taddr, cs[ci], has_c, row_ok, grow, col0, valid);
                     }
                 }
             }
             if (aborted) break;
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(tempty(acc));
+            if (lane == 0) mbar_arrive_cluster(tempty_base + 8u * acc);
         }
     }
 
     // ------------------------------- teardown -------------------------------------
+    if (producer_aborted) {
+        // A B copy of the peer may still be landing after rank 0 stopped expecting it;
+        // give it time before this CTA's shared memory can be released.
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 100000ull) {
+        }
+    }
+    __syncwarp();
     tc_fence_before();
-    __syncthreads();
+    cluster_sync_all();  // both CTAs done with TMEM, barriers and each other's smem
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, kTmemCols);
+        tmem_dealloc_pair(tmem_base, kTmemCols);
     }
 }
 
@@ -616,7 +796,7 @@ int launch_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const
     p.K = K;
     p.nblkK = (K + 31) / 32;
     p.nblkN = (N + 31) / 32;
-    p.num_m_tiles = (M + BM - 1) / BM;
+    p.num_m_tiles = (M + PAIR_M - 1) / PAIR_M;
     p.num_n_tiles = (N + BN - 1) / BN;
     p.num_kb = (K + BK - 1) / BK;
     const bool al_c = C_data == nullptr || (reinterpret_cast<uintptr_t>(C_data) & 15u) == 0;
@@ -636,9 +816,22 @@ int launch_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const
         }
     }
     const int num_tiles = p.num_m_tiles * p.num_n_tiles;
-    const int grid = num_tiles < device_sm_count() ? num_tiles : device_sm_count();
-    gemm_mxfp8_bf16_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(tmap_a, tmap_b, p);
-    cudaError_t e = cudaGetLastError();
+    const int max_clusters = device_sm_count() / 2;
+    const int clusters = num_tiles < max_clusters ? num_tiles : max_clusters;
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_mxfp8_bf16_kernel, tmap_a, tmap_b, p);
     if (e != cudaSuccess) {
         set_last_error("GEMM launch failed: %s", cudaGetErrorString(e));
         return (int)e;

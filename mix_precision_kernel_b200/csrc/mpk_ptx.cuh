@@ -102,8 +102,7 @@ __device__ __forceinline__ void fence_mbar_init()
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar)
 {
-    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}"
-                 :: "r"(bar) : "memory");
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(bar) : "memory");
 }
 
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
@@ -112,13 +111,16 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
                  :: "r"(bar), "r"(bytes) : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
+// One phase test.  If the phase is not complete the thread is suspended in
+// hardware until it completes or `suspend_ns` elapses (no issue slots are spent
+// spinning meanwhile).
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity, uint32_t suspend_ns = 0u)
 {
     uint32_t ok;
     asm volatile("{\n\t.reg .pred p;\n\t"
-                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
                  "selp.u32 %0, 1, 0, p;\n\t}"
-                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+                 : "=r"(ok) : "r"(bar), "r"(parity), "r"(suspend_ns) : "memory");
     return ok != 0;
 }
 
@@ -134,17 +136,17 @@ constexpr int kDevTimeoutBase = 0x100;  // + wait site id
 
 // Bounded wait on an mbarrier phase.  Returns false (and raises the CTA's abort
 // flag and the device status word) if the phase does not complete within
-// timeout_ns, or if another warp of the CTA already aborted.  No wait in this
-// library can spin forever.
+// timeout_ns, or if another warp of the CTA already aborted.  Each test parks the
+// thread for up to 1 ms; no wait in this library can spin forever.
+constexpr uint32_t kSuspendNs = 1000000u;
+
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int* status, int site, uint64_t timeout_ns)
 {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity, kSuspendNs)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
-#pragma unroll 1
-        for (int i = 0; i < 32; ++i)
-            if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait(bar, parity, kSuspendNs)) return true;
         if (*abort_flag) return false;
         if (globaltimer_ns() - t0 > timeout_ns) {
             *abort_flag = 1;
@@ -262,6 +264,121 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int m, int n, bool b_
          | ((b_mn_major ? 1u : 0u) << 16)    // B major
          | ((uint32_t)(n >> 3) << 17)        // N / 8
          | ((uint32_t)(m >> 4) << 24);       // M / 16
+}
+
+
+// ---------------------------------------------------------------------------
+// Thread-block clusters and the 2-CTA (cta_group::2) forms
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id_x()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t nclusters_x()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+// Arrive on an mbarrier that may live in a peer CTA (shared::cluster address).
+// Default (release, CTA-scope) semantics: the data it publishes is shared memory
+// read by the tensor core, which the writer has already made visible to the
+// async proxy with fence.proxy.async.  A cluster-scope release here would also
+// wait for this thread's outstanding global loads (about a microsecond).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr)
+{
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];"
+                 :: "r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                 :: "r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_all()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// TMA load whose completion is signalled on an mbarrier of either CTA of the pair
+// (`bar` is a shared::cluster address).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap, uint32_t bar_cluster,
+                                                 int32_t x, int32_t y)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];"
+        :: "r"(dst), "l"(tmap), "r"(bar_cluster), "r"(x), "r"(y) : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t holder_smem, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(holder_smem), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair()
+{
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;"
+                 :: "r"(taddr), "r"(ncols) : "memory");
+}
+
+// Pair MMA (issued by the even CTA): D[tmem of both CTAs] (+)= A * B, M=256 split
+// 128/128 across the pair, B's N columns split in halves across the pair.
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                 :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+
+// Arrive on the mbarrier at the same offset in every CTA of `cta_mask` once the
+// pair MMAs issued so far complete.
+__device__ __forceinline__ void umma_commit_pair_mc(uint32_t bar, uint16_t cta_mask)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 :: "r"(bar), "h"(cta_mask) : "memory");
+}
+
+// Arrive on a local mbarrier once the pair MMAs issued so far complete.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(bar) : "memory");
+}
+
+// Named barrier over a subset of warps.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads)
+{
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
 }
 
 }  // namespace mpk
