@@ -125,6 +125,34 @@ def test_a_scale_range_exact_bf16(mpk_lib, cuda, scale_byte):
     check_parity(Dd, Ds, O.gold_mx(inp), f"A scale {scale_byte}")
 
 
+@pytest.mark.parametrize("with_nan", [False, True])
+def test_a_exotic_scales_and_nan_codes(mpk_lib, cuda, with_nan):
+    """A scale bytes 0 (scale 0.0), 1-2 (products below BF16's subnormal range),
+    134/135 (the fast-path edge), 247-255 (values beyond FP32/BF16 range, 255 =
+    inf) and NaN codes: the in-kernel dequantization takes the exact path and D
+    matches the FP32 gold, NaN for NaN."""
+    M, N, K = 256, 256, 256
+    inp = O.make_gemm_inputs(M, N, K, seed=77)
+    rng = np.random.default_rng(77)
+    pool = np.array([0, 1, 2, 3, 114, 134, 135, 200, 246, 247, 254, 255], np.uint8)
+    sc = inp["A_scales"].copy()
+    rows = rng.choice(M, 48, replace=False)
+    sc[rows] = rng.choice(pool, (48, sc.shape[1]))
+    inp["A_scales"] = sc
+    if with_nan:
+        d = inp["A_data"].copy()
+        idx = rng.choice(M * K, 20, replace=False)
+        d.ravel()[idx] = rng.choice(np.array([0x7F, 0xFF], np.uint8), 20)
+        inp["A_data"] = d
+    inp["A_deq"] = O.dequantize(inp["A_data"], inp["A_scales"])
+    Dd, Ds = run_gemm(mpk_lib, inp)
+    gold = O.gold_mx(inp)
+    hist = O.mx_ulp_hist(Dd, Ds, gold[1], gold[2])
+    print(f"exotic scales nan={with_nan}: {hist}")
+    assert hist[3] == 0
+    assert hist[0] + hist[1] >= WITHIN_ONE_STEP * sum(hist)
+
+
 def test_k_zero_is_requantized_c(mpk_lib, cuda):
     import torch
 
