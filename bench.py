@@ -310,7 +310,25 @@ def run_gemm_arm(args, world, rank, local, dist):
     flops = 2.0 * M * N * K
     ms_per_step = ms_max / args.steps
     value = world * flops * args.steps / (ms_max / 1e3) / 1e12
-    kernel_tflops = flops / (ms / args.steps / 1e3) / 1e12
+
+    # A step is two launches on `stream`: the A pre-pass (MXFP8 -> BF16 into the
+    # pooled workspace) and the tensor-core kernel.  The pre-pass is timed alone
+    # over as many launches; the tensor-core kernel's time is the difference.
+    ws = torch.empty((M, K), dtype=torch.bfloat16, device="cuda")
+    pre_args = (Ad.data_ptr(), As.data_ptr(), ws.data_ptr(), M, K, sptr)
+    for _ in range(3):
+        L.mpk_mxfp8_dequantize_bf16(*pre_args)
+    barrier_sync(dist)
+    e0.record(stream)
+    for _ in range(args.steps):
+        L.mpk_mxfp8_dequantize_bf16(*pre_args)
+    e1.record(stream)
+    barrier_sync(dist)
+    pre_ms = e0.elapsed_time(e1) / args.steps
+    del ws
+    gemm_ms = ms / args.steps - pre_ms
+    kernel_tflops = flops / (gemm_ms / 1e3) / 1e12
+    step_tflops = flops / (ms / args.steps / 1e3) / 1e12
 
     # end to end through the C ABI with host buffers
     hA = torch.empty_like(Ad, device="cpu").pin_memory(); hA.copy_(Ad)
@@ -342,13 +360,31 @@ def run_gemm_arm(args, world, rank, local, dist):
     e2e_ms = max_over_ranks(dist, e0.elapsed_time(e1))
     e2e_value = world * flops * e2e_steps / (e2e_ms / 1e3) / 1e12
 
+    # Denominator: the burst cuBLAS figure, unless the clock record shows the power
+    # cap acting during the timed region, in which case the sustained figure (the
+    # same GEMM measured back to back under the cap).  Both fractions are reported.
     peaks, peak_src = load_peaks()
-    peak = float(peaks["bf16_tflops"])
-    roofline = {"bound": "tensor", "achieved": round(kernel_tflops, 2), "peak": peak,
+    burst = float(peaks["bf16_tflops"])
+    sustained = float(peaks.get("bf16_tflops_sustained", burst))
+    capped = "sw_power_cap" in clocks["reasons"]
+    peak = sustained if capped else burst
+    hbm = float(peaks["hbm_gbs"])
+    pre_bytes = M * K + M * ((K + 31) // 32) + 2 * M * K
+    roofline = {"bound": "tensor", "kernel": "gemm_bf16a_mxfp8_kernel",
+                "achieved": round(kernel_tflops, 2), "peak": peak,
                 "unit": "TFLOP/s", "frac": round(kernel_tflops / peak, 4),
-                "traffic": load_traffic("gemm_mxfp8_bf16_kernel", args.workload),
-                "peak_source": f"{peak_src} bf16_tflops (burst; kernel timed back to back)",
-                "algorithmic": f"2*M*N*K = {flops:.4e} FLOP per launch"}
+                "traffic": load_traffic("gemm_bf16a_mxfp8_kernel", args.workload),
+                "peak_source": (f"{peak_src} bf16_tflops_sustained (sw_power_cap active in the timed "
+                                f"region)" if capped else f"{peak_src} bf16_tflops (burst)"),
+                "frac_of_burst": round(kernel_tflops / burst, 4),
+                "algorithmic": f"2*M*N*K = {flops:.4e} FLOP per launch",
+                "kernel_ms": round(gemm_ms, 5),
+                "timing": "step time (CUDA events over the timed region) minus the A pre-pass "
+                          "timed alone over the same number of launches",
+                "step_achieved": round(step_tflops, 2), "step_frac": round(step_tflops / peak, 4),
+                "prepass": {"kernel": "mxfp8_dequantize_bf16_flat_kernel", "ms": round(pre_ms, 5),
+                            "bytes": pre_bytes, "achieved_gbs": round(pre_bytes / pre_ms / 1e6, 1),
+                            "frac_of_hbm": round(pre_bytes / pre_ms / 1e6 / hbm, 4)}}
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
@@ -361,8 +397,8 @@ def run_gemm_arm(args, world, rank, local, dist):
                    "parallelism": f"M-slab x{world}, no collective",
                    "l2": f"inputs+outputs {((M*K*33)//32 + 2*K*N + 2*(M*N*33)//32)/2**20:.0f} MiB > "
                          f"126 MiB L2; no flush between steps"},
-        "gpu_launches": args.steps,
-        "pct_of_bf16_peak": round(100.0 * value / world / peak, 2),
+        "gpu_launches": 2 * args.steps,
+        "pct_of_bf16_peak": round(100.0 * value / world / burst, 2),
         "e2e": {"value": round(e2e_value, 3), "unit": "TFLOPS", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
         "roofline": roofline,

@@ -18,13 +18,16 @@
  * Differences from the reference, by design:
  *   - every entry point returns a status code (0 = success) instead of calling
  *     exit() on failure; a detail message is available from mpk_last_error();
- *   - nothing allocates device memory: the launch path is stream-ordered, never
- *     synchronizes the device and can be captured in a CUDA graph;
+ *   - no call synchronizes the device; every launch is stream-ordered;
+ *   - mpk_gemm_mxfp8_bf16 does not cudaMalloc/cudaFree per call: the M*K*2-byte
+ *     workspace of its A pre-pass comes from a library-owned stream-ordered pool
+ *     that stays reserved for reuse (mpk_release_workspace_pool returns it);
  *   - indexing is 64-bit.
  */
 #ifndef MPK_H_
 #define MPK_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -45,10 +48,33 @@ enum {
 /* D = A*B + C.  Replaces gemm_fp8_tensorcore (reference include/gemm_kernels.h:12-16,
  * src/kernels/gemm_fp8_tensorcore.cu:231-249).  Requirements: K % 16 == 0 and
  * N % 8 == 0 (TMA row strides), A_data and B 16-byte aligned.  C_data/C_scales
- * may both be NULL (no C term).  Stream-ordered; allocates nothing. */
+ * may both be NULL (no C term).
+ *
+ * A is dequantized exactly to BF16 by a bandwidth pre-pass into a workspace taken
+ * from the library's pool on `stream`, then the tensor-core kernel streams both
+ * operands by TMA.  While `stream` is being captured into a CUDA graph (or if the
+ * pool cannot supply the workspace) the kernel that converts A on chip runs
+ * instead; it needs no workspace and its D is bit-identical. */
 int mpk_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
                         const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                         uint8_t* D_scales, int M, int N, int K, void* stream);
+
+/* Same computation with a caller-provided workspace: at least
+ * mpk_gemm_workspace_size() bytes (M*K*2), 16-byte aligned, not used by other
+ * work in flight until this call's kernels have finished on `stream`.  With
+ * workspace == NULL the on-chip conversion kernel runs (no workspace at all).
+ * No counterpart in the reference (its launcher allocates its own temporary). */
+int mpk_gemm_mxfp8_bf16_ws(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
+                           const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
+                           uint8_t* D_scales, int M, int N, int K, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* Workspace bytes mpk_gemm_mxfp8_bf16_ws needs for an M x N x K product. */
+int mpk_gemm_workspace_size(int M, int N, int K, size_t* bytes);
+
+/* Returns the current device's pooled GEMM workspace to the driver, once the
+ * work queued on it has finished.  No counterpart in the reference. */
+int mpk_release_workspace_pool(void);
 
 /* float [M][K] -> MXFP8 along K.  Replaces mxfp8_quantize_gpu (reference
  * include/mxfp8_utils.h:38-40, src/quantize/mxfp8_quantize.cu:82-88).  Bit-exact
@@ -60,6 +86,13 @@ int mpk_mxfp8_quantize(const float* input, uint8_t* data, uint8_t* scales, int M
  * include/mxfp8_utils.h:46-47, src/quantize/mxfp8_dequantize.cu:22-29).  Bit-exact. */
 int mpk_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, float* output, int M, int K,
                          void* stream);
+
+/* MXFP8 [M][K] -> BF16 [M][K] (bit patterns, 2-byte aligned output): code x
+ * 2^(scale-127) rounded to nearest even, which is exact for scale bytes >= 3.
+ * This is the A pre-pass of mpk_gemm_mxfp8_bf16.  No counterpart in the reference
+ * (its dequantizer produces FP32 only). */
+int mpk_mxfp8_dequantize_bf16(const uint8_t* data, const uint8_t* scales, void* output, int M, int K,
+                              void* stream);
 
 /* Host-side utilities with the reference's semantics, for building inputs and
  * checking results on the CPU (reference include/mxfp8_utils.h:34-35, :43-44;

@@ -26,6 +26,8 @@ __all__ = [
     "MpkError", "lib", "library_path",
     "gemm_fp8_tensorcore", "mxfp8_quantize_gpu", "mxfp8_dequantize_gpu",
     "mxfp8_quantize_host", "mxfp8_dequantize_host",
+    "gemm_fp8_tensorcore_ws", "gemm_workspace_size", "release_workspace_pool",
+    "mxfp8_dequantize_bf16_gpu",
     "gemm", "quantize", "dequantize", "device_status", "set_wait_timeout_ns", "wait_selftest",
     "MX_BLOCK", "nblk",
 ]
@@ -70,8 +72,13 @@ def lib() -> ctypes.CDLL:
             L = ctypes.CDLL(_LIB_PATH)
             vp, ci, u8p = ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p
             L.mpk_gemm_mxfp8_bf16.argtypes = [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, vp]
+            L.mpk_gemm_mxfp8_bf16_ws.argtypes = [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, vp,
+                                                 ctypes.c_size_t, vp]
+            L.mpk_gemm_workspace_size.argtypes = [ci, ci, ci, ctypes.POINTER(ctypes.c_size_t)]
+            L.mpk_release_workspace_pool.argtypes = []
             L.mpk_mxfp8_quantize.argtypes = [vp, vp, vp, ci, ci, vp]
             L.mpk_mxfp8_dequantize.argtypes = [vp, vp, vp, ci, ci, vp]
+            L.mpk_mxfp8_dequantize_bf16.argtypes = [vp, vp, vp, ci, ci, vp]
             L.mpk_mxfp8_quantize_host.argtypes = [vp, u8p, u8p, ci, ci]
             L.mpk_mxfp8_dequantize_host.argtypes = [u8p, u8p, vp, ci, ci]
             L.mpk_device_status.argtypes = [ctypes.POINTER(ci)]
@@ -81,7 +88,9 @@ def lib() -> ctypes.CDLL:
             L.mpk_status_string.restype = ctypes.c_char_p
             L.mpk_last_error.argtypes = []
             L.mpk_last_error.restype = ctypes.c_char_p
-            for f in ("mpk_gemm_mxfp8_bf16", "mpk_mxfp8_quantize", "mpk_mxfp8_dequantize",
+            for f in ("mpk_gemm_mxfp8_bf16", "mpk_gemm_mxfp8_bf16_ws", "mpk_gemm_workspace_size",
+                      "mpk_release_workspace_pool", "mpk_mxfp8_quantize", "mpk_mxfp8_dequantize",
+                      "mpk_mxfp8_dequantize_bf16",
                       "mpk_mxfp8_quantize_host", "mpk_mxfp8_dequantize_host", "mpk_device_status",
                       "mpk_set_wait_timeout_ns", "mpk_wait_selftest", "mpk_version"):
                 getattr(L, f).restype = ci
@@ -136,6 +145,34 @@ def gemm_fp8_tensorcore(A_data, A_scales, B, C_data, C_scales, D_data, D_scales,
                                      _addr(C_scales), _addr(D_data), _addr(D_scales), M, N, K, s))
 
 
+def gemm_workspace_size(M: int, N: int, K: int) -> int:
+    n = ctypes.c_size_t(0)
+    _check(lib().mpk_gemm_workspace_size(M, N, K, ctypes.byref(n)))
+    return n.value
+
+
+def gemm_fp8_tensorcore_ws(A_data, A_scales, B, C_data, C_scales, D_data, D_scales,
+                           M: int, N: int, K: int, workspace, stream=None) -> None:
+    """gemm_fp8_tensorcore with the A operand dequantized into a caller workspace
+    (a uint8 CUDA tensor of at least gemm_workspace_size(M, N, K) bytes), or,
+    with workspace=None, converted on chip by the GEMM kernel itself."""
+    s = _stream(stream, A_data, D_data)
+    if workspace is None:
+        nbytes = 0
+    elif isinstance(workspace, int):
+        nbytes = 1 << 62
+    else:
+        nbytes = workspace.numel() * workspace.element_size()
+    _check(lib().mpk_gemm_mxfp8_bf16_ws(_addr(A_data), _addr(A_scales), _addr(B), _addr(C_data),
+                                        _addr(C_scales), _addr(D_data), _addr(D_scales), M, N, K,
+                                        _addr(workspace), nbytes, s))
+
+
+def release_workspace_pool() -> None:
+    """Return the current device's pooled GEMM workspace to the driver."""
+    _check(lib().mpk_release_workspace_pool())
+
+
 def mxfp8_quantize_gpu(input, data, scales, M: int, K: int, stream=None) -> None:
     s = _stream(stream, input, data)
     _check(lib().mpk_mxfp8_quantize(_addr(input), _addr(data), _addr(scales), M, K, s))
@@ -144,6 +181,12 @@ def mxfp8_quantize_gpu(input, data, scales, M: int, K: int, stream=None) -> None
 def mxfp8_dequantize_gpu(data, scales, output, M: int, K: int, stream=None) -> None:
     s = _stream(stream, data, output)
     _check(lib().mpk_mxfp8_dequantize(_addr(data), _addr(scales), _addr(output), M, K, s))
+
+
+def mxfp8_dequantize_bf16_gpu(data, scales, output, M: int, K: int, stream=None) -> None:
+    """MXFP8 -> BF16 (the GEMM's A pre-pass); output is a bfloat16 CUDA tensor [M, K]."""
+    s = _stream(stream, data, output)
+    _check(lib().mpk_mxfp8_dequantize_bf16(_addr(data), _addr(scales), _addr(output), M, K, s))
 
 
 def mxfp8_quantize_host(input, data, scales, M: int, K: int) -> None:

@@ -150,15 +150,19 @@ int mpk_set_wait_timeout_ns(uint64_t ns)
     return MPK_SUCCESS;
 }
 
-int mpk_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
-                        const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
-                        uint8_t* D_scales, int M, int N, int K, void* stream)
+static int validate_gemm(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
+                         const uint8_t*& C_data, const uint8_t*& C_scales, uint8_t* D_data,
+                         uint8_t* D_scales, int M, int N, int K, bool& nothing_to_do)
 {
+    nothing_to_do = false;
     if (M < 0 || N < 0 || K < 0) {
         set_last_error("negative size M=%d N=%d K=%d", M, N, K);
         return MPK_ERR_INVALID_VALUE;
     }
-    if (M == 0 || N == 0) return MPK_SUCCESS;
+    if (M == 0 || N == 0) {
+        nothing_to_do = true;
+        return MPK_SUCCESS;
+    }
     if (!D_data || !D_scales || (K > 0 && (!A_data || !A_scales || !B_bf16))) {
         set_last_error("null device pointer");
         return MPK_ERR_INVALID_VALUE;
@@ -167,22 +171,131 @@ int mpk_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const vo
     // (src/kernels/gemm_fp8_tensorcore.cu:188).
     if (!C_data || !C_scales) C_data = nullptr, C_scales = nullptr;
     if (int rc = check_arch()) return rc;
-    if (K == 0) {
-        // A*B is empty: D = MXFP8(C), or MXFP8(0) without C.
-        return from_cuda(launch_mxfp8_requantize(C_data, C_scales, D_data, D_scales, M, N,
-                                                 (cudaStream_t)stream),
-                         "requantize launch");
-    }
-    if (K % 16 != 0 || N % 8 != 0) {
+    if (K > 0 && (K % 16 != 0 || N % 8 != 0)) {
         set_last_error("GEMM needs K %% 16 == 0 and N %% 8 == 0 (TMA row strides); got N=%d K=%d", N, K);
         return MPK_ERR_UNSUPPORTED;
     }
-    if ((reinterpret_cast<uintptr_t>(A_data) & 15u) || (reinterpret_cast<uintptr_t>(B_bf16) & 15u)) {
+    if (K > 0 && ((reinterpret_cast<uintptr_t>(A_data) & 15u) || (reinterpret_cast<uintptr_t>(B_bf16) & 15u))) {
         set_last_error("A_data and B must be 16-byte aligned for TMA");
         return MPK_ERR_MISALIGNED;
     }
+    return MPK_SUCCESS;
+}
+
+// Stream-ordered pool of one device for the A workspace of mpk_gemm_mxfp8_bf16.
+// Its release threshold is unbounded, so after the first call of a given size the
+// workspace is reused without any driver allocation; mpk_release_workspace_pool
+// hands the reserve back.
+namespace {
+std::mutex g_pool_mu;
+cudaMemPool_t g_pools[64] = {};
+}  // namespace
+
+static cudaMemPool_t workspace_pool(bool create)
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    if (!g_pools[dev] && create) {
+        cudaMemPoolProps pp;
+        std::memset(&pp, 0, sizeof(pp));
+        pp.allocType = cudaMemAllocationTypePinned;
+        pp.location.type = cudaMemLocationTypeDevice;
+        pp.location.id = dev;
+        cudaMemPool_t pool = nullptr;
+        if (cudaMemPoolCreate(&pool, &pp) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        uint64_t keep = UINT64_MAX;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        g_pools[dev] = pool;
+    }
+    return g_pools[dev];
+}
+
+int mpk_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
+                        const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
+                        uint8_t* D_scales, int M, int N, int K, void* stream)
+{
+    bool done = false;
+    if (int rc = validate_gemm(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales, M, N, K, done))
+        return rc;
+    if (done) return MPK_SUCCESS;
+    const cudaStream_t st = (cudaStream_t)stream;
+    if (K == 0) {
+        // A*B is empty: D = MXFP8(C), or MXFP8(0) without C.
+        return from_cuda(launch_mxfp8_requantize(C_data, C_scales, D_data, D_scales, M, N, st),
+                         "requantize launch");
+    }
+    // Pre-pass path with the workspace taken from the pool on `stream`.  While the
+    // stream is being captured, or when the pool cannot supply the bytes, the
+    // in-kernel conversion runs instead: it needs no workspace and gives the same D.
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusActive;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) {
+        cudaGetLastError();
+        cs = cudaStreamCaptureStatusActive;
+    }
+    if (cs == cudaStreamCaptureStatusNone) {
+        if (cudaMemPool_t pool = workspace_pool(true)) {
+            void* ws = nullptr;
+            if (cudaMallocFromPoolAsync(&ws, gemm_workspace_bytes(M, K), pool, st) == cudaSuccess) {
+                const int rc = launch_gemm_mxfp8_bf16_prepass(A_data, A_scales, B_bf16, C_data, C_scales,
+                                                              D_data, D_scales, M, N, K, ws, st);
+                const cudaError_t fe = cudaFreeAsync(ws, st);
+                return rc ? rc : from_cuda(fe, "workspace release");
+            }
+            cudaGetLastError();
+        }
+    }
     return launch_gemm_mxfp8_bf16(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales, M, N,
-                                  K, (cudaStream_t)stream);
+                                  K, st);
+}
+
+int mpk_release_workspace_pool(void)
+{
+    cudaMemPool_t pool = workspace_pool(false);
+    if (!pool) return MPK_SUCCESS;
+    return from_cuda(cudaMemPoolTrimTo(pool, 0), "workspace pool trim");
+}
+
+int mpk_gemm_workspace_size(int M, int N, int K, size_t* bytes)
+{
+    if (!bytes || M < 0 || N < 0 || K < 0) return MPK_ERR_INVALID_VALUE;
+    *bytes = gemm_workspace_bytes(M, K);
+    return MPK_SUCCESS;
+}
+
+int mpk_gemm_mxfp8_bf16_ws(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
+                           const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
+                           uint8_t* D_scales, int M, int N, int K, void* workspace,
+                           size_t workspace_bytes, void* stream)
+{
+    bool done = false;
+    if (int rc = validate_gemm(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales, M, N, K, done))
+        return rc;
+    if (done) return MPK_SUCCESS;
+    if (K == 0)
+        return from_cuda(launch_mxfp8_requantize(C_data, C_scales, D_data, D_scales, M, N,
+                                                 (cudaStream_t)stream),
+                         "requantize launch");
+    if (!workspace)
+        return launch_gemm_mxfp8_bf16(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales, M,
+                                      N, K, (cudaStream_t)stream);
+    const size_t need = gemm_workspace_bytes(M, K);
+    if (workspace_bytes < need) {
+        set_last_error("workspace of %zu bytes needed (M*K*2), got %zu", need, workspace_bytes);
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (reinterpret_cast<uintptr_t>(workspace) & 15u) {
+        set_last_error("workspace must be 16-byte aligned");
+        return MPK_ERR_MISALIGNED;
+    }
+    return launch_gemm_mxfp8_bf16_prepass(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales,
+                                          M, N, K, workspace, (cudaStream_t)stream);
 }
 
 int mpk_mxfp8_quantize(const float* input, uint8_t* data, uint8_t* scales, int M, int K, void* stream)
@@ -216,6 +329,27 @@ int mpk_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, float* outp
     if (int rc = check_arch()) return rc;
     return from_cuda(launch_mxfp8_dequantize(data, scales, output, M, K, (cudaStream_t)stream),
                      "dequantize launch");
+}
+
+int mpk_mxfp8_dequantize_bf16(const uint8_t* data, const uint8_t* scales, void* output, int M, int K,
+                              void* stream)
+{
+    if (M < 0 || K < 0) {
+        set_last_error("negative size M=%d K=%d", M, K);
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (M == 0 || K == 0) return MPK_SUCCESS;
+    if (!data || !scales || !output) {
+        set_last_error("null device pointer");
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (reinterpret_cast<uintptr_t>(output) & 1u) {
+        set_last_error("BF16 output must be 2-byte aligned");
+        return MPK_ERR_MISALIGNED;
+    }
+    if (int rc = check_arch()) return rc;
+    return from_cuda(launch_mxfp8_dequantize_bf16(data, scales, output, M, K, (cudaStream_t)stream),
+                     "dequantize-bf16 launch");
 }
 
 int mpk_mxfp8_quantize_host(const float* input, uint8_t* data, uint8_t* scales, int M, int K)

@@ -14,6 +14,7 @@
 // K = 100, or unaligned pointers): one warp per (row, block), one element per lane.
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <cuda_bf16.h>
 
 #include "mpk_ptx.cuh"
 #include "mpk_internal.h"
@@ -137,6 +138,91 @@ mxfp8_dequantize_elem_kernel(const uint8_t* __restrict__ data, const uint8_t* __
     }
 }
 
+
+// ------------------------- dequantize to BF16 (GEMM A) -------------------------
+//
+// MXFP8 [M][K] -> BF16 [M][K], exact: code x 2^(s-127) has at most 4 significant
+// bits and BF16 keeps FP32's exponent range, so the product is representable for
+// every scale byte except 1 and 2 (whose smallest products sit below BF16's
+// subnormal range and are rounded to nearest even, as cvt.rn does).  Byte 0 gives
+// 0 and byte 255 gives +-inf (NaN for code 0), as the reference's e8m0_to_float.
+//
+// Fast path per 8 codes sharing a scale byte in 3..134 with no NaN code: integer
+// bit placement of each code as BF16 code x 2^-120, then one exact mul.rn.bf16x2
+// by 2^(s-7).  Anything else: E4M3 -> f32 hardware conversion, FP32 multiply,
+// cvt.rn to BF16.
+__device__ __forceinline__ uint32_t prmt_b32(uint32_t a, uint32_t b, uint32_t sel)
+{
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b)
+{
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint4 e4m3x8_to_bf16x8(uint2 c, uint32_t s)
+{
+    const uint32_t in[2] = {c.x, c.y};
+    uint32_t out[4];
+    const uint32_t wm0 = in[0] & 0x7F7F7F7Fu, wm1 = in[1] & 0x7F7F7F7Fu;
+    const uint32_t nan_probe = ((wm0 + 0x01010101u) | (wm1 + 0x01010101u)) & 0x80808080u;
+    if ((s - 3u) <= 131u && nan_probe == 0u) {
+        uint32_t f = (s + 120u) << 7;
+        f |= f << 16;
+        const uint32_t wm[2] = {wm0, wm1};
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+            const uint32_t ws = in[w] & 0x80808080u;
+            out[2 * w] = bf16x2_mul(prmt_b32(wm[w], 0u, 0x4140u) * 16u + prmt_b32(ws, 0u, 0x1404u), f);
+            out[2 * w + 1] = bf16x2_mul(prmt_b32(wm[w], 0u, 0x4342u) * 16u + prmt_b32(ws, 0u, 0x3424u), f);
+        }
+    } else {
+        const float sc = e8m0_to_f32(s);
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float2 f = e4m3x2_to_f32x2(in[w] >> (16 * h));
+                uint32_t packed;
+                asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed) : "f"(f.y * sc), "f"(f.x * sc));
+                out[2 * w + h] = packed;
+            }
+        }
+    }
+    return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// K % 32 == 0, 8-byte aligned codes, 16-byte aligned output: flat run of blocks.
+__global__ void __launch_bounds__(kCodecThreads)
+mxfp8_dequantize_bf16_flat_kernel(const uint8_t* __restrict__ data, const uint8_t* __restrict__ scales,
+                                  uint16_t* __restrict__ out, int64_t n_octets)
+{
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < n_octets; o += stride) {
+        const uint2 c = __ldcs(reinterpret_cast<const uint2*>(data) + o);
+        const uint32_t s = __ldg(scales + (o >> 2));
+        reinterpret_cast<uint4*>(out)[o] = e4m3x8_to_bf16x8(c, s);
+    }
+}
+
+// Any shape: one element per thread.
+__global__ void __launch_bounds__(kCodecThreads)
+mxfp8_dequantize_bf16_elem_kernel(const uint8_t* __restrict__ data, const uint8_t* __restrict__ scales,
+                                  uint16_t* __restrict__ out, int64_t M, int64_t K, int64_t nblk)
+{
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M * K; i += stride) {
+        const int64_t row = i / K, k = i % K;
+        const float v = e4m3x2_to_f32x2(data[i]).x * e8m0_to_f32(scales[row * nblk + k / 32]);
+        out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    }
+}
+
 // ------------------------------- launchers ---------------------------------
 
 static int codec_grid(int64_t work_items)
@@ -177,6 +263,22 @@ cudaError_t launch_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, 
     } else {
         mxfp8_dequantize_elem_kernel<<<codec_grid(M * K), kCodecThreads, 0, stream>>>(
             data, scales, out, M, K, nblk);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mxfp8_dequantize_bf16(const uint8_t* data, const uint8_t* scales, void* out,
+                                         int64_t M, int64_t K, cudaStream_t stream)
+{
+    const int64_t nblk = (K + 31) / 32;
+    if (M == 0 || K == 0) return cudaSuccess;
+    uint16_t* o = static_cast<uint16_t*>(out);
+    if (K % 32 == 0 && aligned16(out) && (reinterpret_cast<uintptr_t>(data) & 7u) == 0) {
+        const int64_t no = M * K / 8;
+        mxfp8_dequantize_bf16_flat_kernel<<<codec_grid(no), kCodecThreads, 0, stream>>>(data, scales, o, no);
+    } else {
+        mxfp8_dequantize_bf16_elem_kernel<<<codec_grid(M * K), kCodecThreads, 0, stream>>>(
+            data, scales, o, M, K, nblk);
     }
     return cudaGetLastError();
 }

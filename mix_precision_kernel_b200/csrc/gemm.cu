@@ -74,11 +74,31 @@ constexpr int kTransformGroups = MPK_TRANSFORM_GROUPS;
 static_assert(kTransformGroups == 1 || kTransformGroups == 2 || kTransformGroups == 4, "1, 2 or 4");
 constexpr int kTransformWarps = 4 * kTransformGroups;
 constexpr int kEpilogueWarps = 4;
-constexpr int kFirstTransformWarp = 3;
+// Warpgroup-aligned layout: warps 0-3 control (B producer, MMA/TMEM, A-code
+// producer, one idle), then the transform groups, then the epilogue warpgroup.
+constexpr int kFirstTransformWarp = 4;
+#ifndef MPK_B_PRODUCER_WARP
+#define MPK_B_PRODUCER_WARP 0
+#endif
+constexpr int kBProducerWarp = MPK_B_PRODUCER_WARP;  // 0 or 3 (the other one idles)
+static_assert(kBProducerWarp == 0 || kBProducerWarp == 3, "warp 0 or 3");
 constexpr int kFirstEpilogueWarp = kFirstTransformWarp + kTransformWarps;
 constexpr int kThreads = 32 * (kFirstEpilogueWarp + kEpilogueWarps);
+// Register split per warpgroup (setmaxnreg): the launch gives every thread
+// kLaunchRegs; control warps drop to kCtrlRegs, transform warps to kXformRegs and
+// the epilogue rises to kEpiRegs.  The sum never exceeds the launch allocation
+// (checked below), and the launcher verifies the compiled register count before
+// it launches, so setmaxnreg.inc can always be satisfied.
+constexpr int kLaunchRegs = (65536 / kThreads) / 8 * 8 > 255 ? 248 : (65536 / kThreads) / 8 * 8;
+constexpr int kCtrlRegs = 40;
+constexpr int kXformRegs = kTransformGroups == 4 ? 72 : kLaunchRegs;
+constexpr int kEpiRegs = (kThreads * kLaunchRegs - 128 * kCtrlRegs - 32 * kTransformWarps * kXformRegs) /
+                         128 / 8 * 8 > 248 ? 248
+                       : (kThreads * kLaunchRegs - 128 * kCtrlRegs - 32 * kTransformWarps * kXformRegs) / 128 / 8 * 8;
+static_assert(128 * kCtrlRegs + 32 * kTransformWarps * kXformRegs + 128 * kEpiRegs <= kThreads * kLaunchRegs,
+              "register split exceeds the launch allocation");
 #ifndef MPK_C_PREFETCH
-#define MPK_C_PREFETCH (kTransformGroups <= 2 ? 4 : 2)
+#define MPK_C_PREFETCH (kEpiRegs >= 160 ? 8 : 4)
 #endif
 constexpr int kCPrefetch = MPK_C_PREFETCH;  // C chunks (32 columns) prefetched per round
 
@@ -299,7 +319,108 @@ __device__ __noinline__ void epilogue_ragged_chunk(const Params& p, uint32_t tad
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+// Epilogue of one CTA (4 warps, one thread per accumulator row): for every tile of
+// this cluster, wait for the accumulator, add the dequantized C, quantize D to MXFP8
+// along N and store it, then release the accumulator on rank 0's tempty barrier.
+__device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base, uint32_t tfull0,
+                                         uint32_t tempty_base, int cluster, int nclusters,
+                                         uint32_t rank, int warp, int lane, volatile int* abort_flag)
+{
+    const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+    auto tfull = [&](int a) { return tfull0 + 8u * a; };
+    const int quad = warp & 3;                 // TMEM lanes this warp may access
+    const int r = quad * 32 + lane;            // accumulator row within this CTA's tile
+    const bool has_c = p.C_data != nullptr;
+    bool aborted = false;
+    int it = 0;
+    for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
+        int m0, n0;
+        tile_coords(p, tile, m0, n0);
+        const int acc = it & 1;
+        const uint32_t acc_ph = (uint32_t)(it >> 1) & 1u;
+        const int64_t grow = (int64_t)m0 + BM * (int)rank + r;
+        const bool row_ok = grow < p.M;
+        const int nchunks = min(BN / 32, (p.N - n0 + 31) / 32);
+        bool full_seen = false;
+#pragma unroll
+        for (int c0 = 0; c0 < BN / 32; c0 += kCPrefetch) {
+            if (c0 >= nchunks) break;  // warp-uniform
+            // Prefetch this row's C codes and scales for the next kCPrefetch chunks
+            // (before the accumulator is ready, so the loads overlap the mainloop).
+            uint4 cq[kCPrefetch][2];
+            uint32_t cs[kCPrefetch];
+#pragma unroll
+            for (int ci = 0; ci < kCPrefetch; ++ci) {
+                const int c = c0 + ci;
+                cq[ci][0] = cq[ci][1] = make_uint4(0u, 0u, 0u, 0u);
+                cs[ci] = 0u;
+                const int col0 = n0 + 32 * c;
+                if (has_c && row_ok && c < nchunks) {
+                    cs[ci] = __ldg(p.C_scales + grow * p.nblkN + col0 / 32);
+                    if (p.vec_cd && col0 + 32 <= p.N) {
+                        const uint4* src = reinterpret_cast<const uint4*>(p.C_data + grow * p.N + col0);
+                        cq[ci][0] = __ldg(src);
+                        cq[ci][1] = __ldg(src + 1);
+                    }
+                }
+            }
+            if (!full_seen) {
+                if (!mbar_wait(tfull(acc), acc_ph, abort_flag, p.status, kSiteTmemFull, p.timeout_ns)) {
+                    aborted = true;
+                    break;
+                }
+                tc_fence_after();
+                full_seen = true;
+            }
+#pragma unroll
+            for (int ci = 0; ci < kCPrefetch; ++ci) {
+                const int c = c0 + ci;
+                if (c >= nchunks) break;  // warp-uniform: tcgen05.ld is warp-collective
+                const int col0 = n0 + 32 * c;
+                const int valid = min(32, p.N - col0);
+                const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + 32 * c);
+                if (valid == 32 && p.vec_cd) {
+                    uint32_t raw[32];
+                    tmem_ld_32x32b_x32(taddr, raw);
+                    tmem_ld_wait();
+                    float v[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]);
+                    if (has_c) {
+                        const float sc = e8m0_to_f32(cs[ci]);
+                        const uint32_t cw[8] = {cq[ci][0].x, cq[ci][0].y, cq[ci][0].z, cq[ci][0].w,
+                                                cq[ci][1].x, cq[ci][1].y, cq[ci][1].z, cq[ci][1].w};
+#pragma unroll
+                        for (int w = 0; w < 8; ++w) {
+                            const float2 lo = e4m3x2_to_f32x2(cw[w]);
+                            const float2 hi = e4m3x2_to_f32x2(cw[w] >> 16);
+                            v[4 * w + 0] += lo.x * sc;
+                            v[4 * w + 1] += lo.y * sc;
+                            v[4 * w + 2] += hi.x * sc;
+                            v[4 * w + 3] += hi.y * sc;
+                        }
+                    }
+                    uint4 d0, d1;
+                    const uint32_t sd = quantize_block32(v, d0, d1);
+                    if (row_ok) {
+                        uint4* dst = reinterpret_cast<uint4*>(p.D_data + grow * p.N + col0);
+                        dst[0] = d0;
+                        dst[1] = d1;
+                        p.D_scales[grow * p.nblkN + col0 / 32] = (uint8_t)sd;
+                    }
+                } else {
+                    epilogue_ragged_chunk(p, taddr, cs[ci], has_c, row_ok, grow, col0, valid);
+                }
+            }
+        }
+        if (aborted) break;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(tempty_base + 8u * acc);
+    }
+    }
+
+__global__ void __maxnreg__(kLaunchRegs)
 gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                        const __grid_constant__ CUtensorMap tmap_b, const Params p)
 {
@@ -359,7 +480,9 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
     const uint32_t tmem_base = *tmem_holder;
     bool producer_aborted = false;
 
-    if (warp == 0) {
+    if (warp < kFirstTransformWarp) {
+    setmaxnreg_dec<kCtrlRegs>();
+    if (warp == kBProducerWarp) {
         // ---------------------------- B producer (TMA) ----------------------------
         if (lane == 0) {
             prefetch_tmap(&tmap_b);
@@ -479,7 +602,10 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
             umma_commit_pair(drain);
             mbar_wait(drain, 0, never_abort, nullptr, 0, kDrainTimeoutNs);
         }
+    }
+    // warp 3: idle (keeps the transform and epilogue warpgroups aligned)
     } else if (warp < kFirstEpilogueWarp) {
+        if constexpr (kXformRegs < kLaunchRegs) setmaxnreg_dec<kXformRegs>();
         // ------------------------------- transform --------------------------------
         // Group g (4 warps, one thread per row of this CTA's A tile) converts the
         // K-steps kb with kb % G == g.  A warp covers 32 consecutive rows, which keeps
@@ -555,98 +681,10 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
             }
         }
     } else {
+        setmaxnreg_inc<kEpiRegs>();
         // -------------------------------- epilogue --------------------------------
-        const int quad = warp & 3;                 // TMEM lanes this warp may access
-        const int r = quad * 32 + lane;            // accumulator row within this CTA's tile
-        const bool has_c = p.C_data != nullptr;
-        const uint32_t tempty_base = mapa_shared(tempty(0), 0);
-        bool aborted = false;
-        int it = 0;
-        for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
-            int m0, n0;
-            tile_coords(p, tile, m0, n0);
-            const int acc = it & 1;
-            const uint32_t acc_ph = (uint32_t)(it >> 1) & 1u;
-            const int64_t grow = (int64_t)m0 + BM * (int)rank + r;
-            const bool row_ok = grow < p.M;
-            const int nchunks = min(BN / 32, (p.N - n0 + 31) / 32);
-            bool full_seen = false;
-#pragma unroll
-            for (int c0 = 0; c0 < BN / 32; c0 += kCPrefetch) {
-                if (c0 >= nchunks) break;  // warp-uniform
-                // Prefetch this row's C codes and scales for the next kCPrefetch chunks
-                // (before the accumulator is ready, so the loads overlap the mainloop).
-                uint4 cq[kCPrefetch][2];
-                uint32_t cs[kCPrefetch];
-#pragma unroll
-                for (int ci = 0; ci < kCPrefetch; ++ci) {
-                    const int c = c0 + ci;
-                    cq[ci][0] = cq[ci][1] = make_uint4(0u, 0u, 0u, 0u);
-                    cs[ci] = 0u;
-                    const int col0 = n0 + 32 * c;
-                    if (has_c && row_ok && c < nchunks) {
-                        cs[ci] = __ldg(p.C_scales + grow * p.nblkN + col0 / 32);
-                        if (p.vec_cd && col0 + 32 <= p.N) {
-                            const uint4* src = reinterpret_cast<const uint4*>(p.C_data + grow * p.N + col0);
-                            cq[ci][0] = __ldg(src);
-                            cq[ci][1] = __ldg(src + 1);
-                        }
-                    }
-                }
-                if (!full_seen) {
-                    if (!mbar_wait(tfull(acc), acc_ph, abort_flag, p.status, kSiteTmemFull, p.timeout_ns)) {
-                        aborted = true;
-                        break;
-                    }
-                    tc_fence_after();
-                    full_seen = true;
-                }
-#pragma unroll
-                for (int ci = 0; ci < kCPrefetch; ++ci) {
-                    const int c = c0 + ci;
-                    if (c >= nchunks) break;  // warp-uniform: tcgen05.ld is warp-collective
-                    const int col0 = n0 + 32 * c;
-                    const int valid = min(32, p.N - col0);
-                    const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + 32 * c);
-                    if (valid == 32 && p.vec_cd) {
-                        uint32_t raw[32];
-                        tmem_ld_32x32b_x32(taddr, raw);
-                        tmem_ld_wait();
-                        float v[32];
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]);
-                        if (has_c) {
-                            const float sc = e8m0_to_f32(cs[ci]);
-                            const uint32_t cw[8] = {cq[ci][0].x, cq[ci][0].y, cq[ci][0].z, cq[ci][0].w,
-                                                    cq[ci][1].x, cq[ci][1].y, cq[ci][1].z, cq[ci][1].w};
-#pragma unroll
-                            for (int w = 0; w < 8; ++w) {
-                                const float2 lo = e4m3x2_to_f32x2(cw[w]);
-                                const float2 hi = e4m3x2_to_f32x2(cw[w] >> 16);
-                                v[4 * w + 0] += lo.x * sc;
-                                v[4 * w + 1] += lo.y * sc;
-                                v[4 * w + 2] += hi.x * sc;
-                                v[4 * w + 3] += hi.y * sc;
-                            }
-                        }
-                        uint4 d0, d1;
-                        const uint32_t sd = quantize_block32(v, d0, d1);
-                        if (row_ok) {
-                            uint4* dst = reinterpret_cast<uint4*>(p.D_data + grow * p.N + col0);
-                            dst[0] = d0;
-                            dst[1] = d1;
-                            p.D_scales[grow * p.nblkN + col0 / 32] = (uint8_t)sd;
-                        }
-                    } else {
-                        epilogue_ragged_chunk(p, taddr, cs[ci], has_c, row_ok, grow, col0, valid);
-                    }
-                }
-            }
-            if (aborted) break;
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(tempty_base + 8u * acc);
-        }
+        run_epilogue(p, tmem_base, tfull(0), mapa_shared(tempty(0), 0), cluster, nclusters, rank, warp,
+                     lane, abort_flag);
     }
 
     // ------------------------------- teardown -------------------------------------
@@ -660,6 +698,181 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
     __syncwarp();
     tc_fence_before();
     cluster_sync_all();  // both CTAs done with TMEM, barriers and each other's smem
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, kTmemCols);
+    }
+}
+
+
+// ============================================================================
+// BF16-A variant: A is dequantized to BF16 in HBM by a bandwidth pre-pass
+// (launch_mxfp8_dequantize_bf16, exact) and streamed by TMA like B, so the
+// mainloop has no transform on its critical path.  Same clusters, tiles, pair
+// MMA and epilogue as above; per CTA and K-step the ring holds the CTA's 128 x 64
+// BF16 A rows (16 KiB, 128-byte swizzle = the UMMA K-major layout) and its 64 x 128
+// B half (16 KiB), both completing on rank 0's full barrier.
+//
+// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer (rank 0), 2-3 idle, 4-7 epilogue.
+// ============================================================================
+#ifndef MPK_P_STAGES
+#define MPK_P_STAGES 7
+#endif
+constexpr int P_STAGES = MPK_P_STAGES;
+constexpr int P_THREADS = 256;
+constexpr int P_FIRST_EPI_WARP = 4;
+constexpr int P_OFF_B = 0;
+constexpr int P_OFF_A = P_OFF_B + P_STAGES * B_BYTES;
+constexpr int P_OFF_BAR = P_OFF_A + P_STAGES * A16_BYTES;
+// barriers: full[S], empty[S], tfull[2], tempty[2], drain
+constexpr int P_NUM_BARS = 2 * P_STAGES + 5;
+constexpr int P_OFF_MISC = P_OFF_BAR + P_NUM_BARS * 8;
+constexpr int P_SMEM_BYTES = P_OFF_MISC + 16 + 1024;
+static_assert(P_SMEM_BYTES <= 232448, "exceeds the sm_100 per-block shared memory limit");
+constexpr uint32_t P_TX_BYTES = 2 * (A16_BYTES + B_BYTES);  // both CTAs' A and B per stage
+
+__global__ void __launch_bounds__(P_THREADS, 1)
+gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
+                        const __grid_constant__ CUtensorMap tmap_b, const Params p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bar0 = sbase + P_OFF_BAR;
+    auto full = [&](int s) { return bar0 + 8u * s; };
+    auto empty = [&](int s) { return bar0 + 8u * (P_STAGES + s); };
+    auto tfull = [&](int a) { return bar0 + 8u * (2 * P_STAGES + a); };
+    auto tempty = [&](int a) { return bar0 + 8u * (2 * P_STAGES + 2 + a); };
+    const uint32_t drain = bar0 + 8u * (2 * P_STAGES + 4);
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + P_OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + P_OFF_MISC + 4);
+    volatile int* never_abort = reinterpret_cast<volatile int*>(smem + P_OFF_MISC + 8);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int cluster = (int)cluster_id_x();
+    const int nclusters = (int)nclusters_x();
+    const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P_STAGES; ++s) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull(a), 1);
+            mbar_init(tempty(a), 2 * kEpilogueWarps);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        *never_abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(tmem_holder), kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+    bool producer_aborted = false;
+
+    if (warp == 0) {
+        // ------------------------ TMA producer (A and B) -------------------------
+        if (lane == 0) {
+            prefetch_tmap(&tmap_a16);
+            prefetch_tmap(&tmap_b);
+            int s = 0;
+            uint32_t ph = 0;
+            int issued = 0;
+            bool ok = true;
+            for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
+                int m0, n0;
+                tile_coords(p, tile, m0, n0);
+                const int row0 = m0 + BM * (int)rank;
+                const int col0 = n0 + BN_HALF * (int)rank;
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, p.status, kSiteEmpty, p.timeout_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    if (rank == 0) mbar_arrive_expect_tx(full(s), P_TX_BYTES);
+                    const uint32_t fb = mapa_shared(full(s), 0);
+                    tma_load_2d_pair(sbase + P_OFF_A + s * A16_BYTES, &tmap_a16, fb, kb * BK, row0);
+#pragma unroll
+                    for (int j = 0; j < BN_HALF / 64; ++j)
+                        tma_load_2d_pair(sbase + P_OFF_B + s * B_BYTES + j * B_BOX_BYTES, &tmap_b, fb,
+                                         col0 + 64 * j, kb * BK);
+                    ++issued;
+                    if (++s == P_STAGES) { s = 0; ph ^= 1u; }
+                }
+            }
+            if (!ok) {
+                producer_aborted = true;
+                const int outstanding = issued < P_STAGES ? issued : P_STAGES;
+                int ss = s;
+                uint32_t pp = ph;
+                for (int i = 0; i < outstanding; ++i) {
+                    if (--ss < 0) { ss = P_STAGES - 1; pp ^= 1u; }
+                    if (rank == 0) mbar_wait(full(ss), pp, never_abort, nullptr, 0, kDrainTimeoutNs);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // --------------------------- MMA issuer (rank 0) ---------------------------
+        if (rank == 0 && lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            int it = 0;
+            bool ok = true;
+            for (int tile = cluster; ok && tile < num_tiles; tile += nclusters, ++it) {
+                const int acc = it & 1;
+                const uint32_t acc_ph = (uint32_t)(it >> 1) & 1u;
+                if (!mbar_wait(tempty(acc), acc_ph ^ 1u, abort_flag, p.status, kSiteTmemEmpty,
+                               p.timeout_ns)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(full(s), ph, abort_flag, p.status, kSiteFullB, p.timeout_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = sbase + P_OFF_A + s * A16_BYTES;
+                    const uint32_t b_addr = sbase + P_OFF_B + s * B_BYTES;
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; ++k) {
+                        const uint64_t adesc = umma_smem_desc_sw128(a_addr + k * UMMA_K * 2, 16, 1024);
+                        const uint64_t bdesc = umma_smem_desc_sw128(b_addr + k * UMMA_K * 128, B_BOX_BYTES, 1024);
+                        umma_bf16_pair(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0 ? 1u : 0u);
+                    }
+                    umma_commit_pair_mc(empty(s), 0x3);
+                    if (++s == P_STAGES) { s = 0; ph ^= 1u; }
+                }
+                if (!ok) break;
+                umma_commit_pair_mc(tfull(acc), 0x3);
+            }
+            umma_commit_pair(drain);
+            mbar_wait(drain, 0, never_abort, nullptr, 0, kDrainTimeoutNs);
+        }
+    } else if (warp >= P_FIRST_EPI_WARP) {
+        run_epilogue(p, tmem_base, tfull(0), mapa_shared(tempty(0), 0), cluster, nclusters, rank, warp,
+                     lane, abort_flag);
+    }
+
+    if (producer_aborted) {
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 100000ull) {
+        }
+    }
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync_all();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc_pair(tmem_base, kTmemCols);
@@ -695,6 +908,7 @@ std::mutex g_mu;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 int* g_status_ptr[64] = {};
 bool g_smem_attr_set[64] = {};
+bool g_regs_checked[64] = {};
 
 int get_device(int& dev)
 {
@@ -763,27 +977,23 @@ int encode_2d(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* map, CUtensorM
 
 }  // namespace
 
-int launch_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const void* B,
-                           const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
-                           uint8_t* D_scales, int M, int N, int K, cudaStream_t stream)
+namespace {
+
+// Shared host setup of both GEMM kernels: device checks, status word, B tensor map
+// and the kernel parameters.
+int gemm_setup(const uint8_t* A_scales, const void* B, const uint8_t* C_data, const uint8_t* C_scales,
+               uint8_t* D_data, uint8_t* D_scales, int M, int N, int K, int& dev,
+               PFN_cuTensorMapEncodeTiled_v12000& enc, CUtensorMap& tmap_b, gemm::Params& p)
 {
     using namespace gemm;
-    int dev = 0, rc = get_device(dev);
+    int rc = get_device(dev);
     if (rc) return rc;
     int* status = nullptr;
     if ((rc = status_ptr(dev, &status))) return rc;
-    PFN_cuTensorMapEncodeTiled_v12000 enc;
     if ((rc = get_encoder(&enc))) return rc;
-
-    CUtensorMap tmap_a, tmap_b;
-    if ((rc = encode_2d(enc, &tmap_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, A_data, (uint64_t)K, (uint64_t)M,
-                        (uint64_t)K, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
-        return rc;
     if ((rc = encode_2d(enc, &tmap_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, B, (uint64_t)N, (uint64_t)K,
                         (uint64_t)N * 2, 64, BK, CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
-
-    Params p;
     p.A_scales = A_scales;
     p.C_data = C_data;
     p.C_scales = C_scales;
@@ -802,27 +1012,20 @@ int launch_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const
     const bool al_c = C_data == nullptr || (reinterpret_cast<uintptr_t>(C_data) & 15u) == 0;
     const bool al_d = (reinterpret_cast<uintptr_t>(D_data) & 15u) == 0;
     p.vec_cd = (N % 16 == 0 && al_c && al_d) ? 1 : 0;
+    return MPK_SUCCESS;
+}
 
-    {
-        std::lock_guard<std::mutex> lk(g_mu);
-        if (!g_smem_attr_set[dev]) {
-            cudaError_t e = cudaFuncSetAttribute(gemm_mxfp8_bf16_kernel,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-            if (e != cudaSuccess) {
-                set_last_error("cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
-                return (int)e;
-            }
-            g_smem_attr_set[dev] = true;
-        }
-    }
+template <typename Kernel>
+int launch_pair_kernel(Kernel kernel, int smem_bytes, int threads, const CUtensorMap& tmap_a,
+                       const CUtensorMap& tmap_b, const gemm::Params& p, cudaStream_t stream)
+{
     const int num_tiles = p.num_m_tiles * p.num_n_tiles;
     const int max_clusters = device_sm_count() / 2;
     const int clusters = num_tiles < max_clusters ? num_tiles : max_clusters;
-
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.dynamicSmemBytes = smem_bytes;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -831,12 +1034,94 @@ int launch_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_mxfp8_bf16_kernel, tmap_a, tmap_b, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmap_a, tmap_b, p);
     if (e != cudaSuccess) {
         set_last_error("GEMM launch failed: %s", cudaGetErrorString(e));
         return (int)e;
     }
     return MPK_SUCCESS;
+}
+
+int ensure_smem_attr(const void* kernel, int bytes, bool* flag)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!*flag) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e != cudaSuccess) {
+            set_last_error("cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+            return (int)e;
+        }
+        *flag = true;
+    }
+    return MPK_SUCCESS;
+}
+
+bool g_smem_attr_bf16a[64] = {};
+
+}  // namespace
+
+size_t gemm_workspace_bytes(int M, int K) { return (size_t)M * (size_t)K * 2u; }
+
+int launch_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const void* B,
+                           const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
+                           uint8_t* D_scales, int M, int N, int K, cudaStream_t stream)
+{
+    using namespace gemm;
+    int dev = 0;
+    PFN_cuTensorMapEncodeTiled_v12000 enc;
+    CUtensorMap tmap_a, tmap_b;
+    Params p;
+    int rc = gemm_setup(A_scales, B, C_data, C_scales, D_data, D_scales, M, N, K, dev, enc, tmap_b, p);
+    if (rc) return rc;
+    if ((rc = encode_2d(enc, &tmap_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, A_data, (uint64_t)K, (uint64_t)M,
+                        (uint64_t)K, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
+        return rc;
+    if ((rc = ensure_smem_attr((const void*)gemm_mxfp8_bf16_kernel, SMEM_BYTES, &g_smem_attr_set[dev])))
+        return rc;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!g_regs_checked[dev]) {
+            cudaFuncAttributes fa;
+            cudaError_t e = cudaFuncGetAttributes(&fa, gemm_mxfp8_bf16_kernel);
+            if (e != cudaSuccess) {
+                set_last_error("cudaFuncGetAttributes failed: %s", cudaGetErrorString(e));
+                return (int)e;
+            }
+            // The setmaxnreg split assumes exactly kLaunchRegs per thread at launch.
+            if (fa.numRegs != kLaunchRegs) {
+                set_last_error("GEMM kernel compiled with %d registers per thread, expected %d",
+                               fa.numRegs, kLaunchRegs);
+                return MPK_ERR_UNSUPPORTED;
+            }
+            g_regs_checked[dev] = true;
+        }
+    }
+    return launch_pair_kernel(gemm_mxfp8_bf16_kernel, SMEM_BYTES, kThreads, tmap_a, tmap_b, p, stream);
+}
+
+int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scales, const void* B,
+                                   const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
+                                   uint8_t* D_scales, int M, int N, int K, void* workspace,
+                                   cudaStream_t stream)
+{
+    using namespace gemm;
+    int dev = 0;
+    PFN_cuTensorMapEncodeTiled_v12000 enc;
+    CUtensorMap tmap_a16, tmap_b;
+    Params p;
+    int rc = gemm_setup(A_scales, B, C_data, C_scales, D_data, D_scales, M, N, K, dev, enc, tmap_b, p);
+    if (rc) return rc;
+    if ((rc = encode_2d(enc, &tmap_a16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, workspace, (uint64_t)K,
+                        (uint64_t)M, (uint64_t)K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return rc;
+    if ((rc = ensure_smem_attr((const void*)gemm_bf16a_mxfp8_kernel, P_SMEM_BYTES, &g_smem_attr_bf16a[dev])))
+        return rc;
+    cudaError_t e = launch_mxfp8_dequantize_bf16(A_data, A_scales, workspace, M, K, stream);
+    if (e != cudaSuccess) {
+        set_last_error("A pre-pass launch failed: %s", cudaGetErrorString(e));
+        return (int)e;
+    }
+    return launch_pair_kernel(gemm_bf16a_mxfp8_kernel, P_SMEM_BYTES, P_THREADS, tmap_a16, tmap_b, p, stream);
 }
 
 int read_and_clear_device_status(int* value)

@@ -16,6 +16,9 @@ cudaError_t launch_mxfp8_quantize(const float* in, uint8_t* data, uint8_t* scale
                                   int64_t K, cudaStream_t stream);
 cudaError_t launch_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, float* out,
                                     int64_t M, int64_t K, cudaStream_t stream);
+// MXFP8 [M][K] -> BF16 [M][K] (exact for scale bytes other than 1 and 2).
+cudaError_t launch_mxfp8_dequantize_bf16(const uint8_t* data, const uint8_t* scales, void* out,
+                                         int64_t M, int64_t K, cudaStream_t stream);
 // D = MXFP8(dequant(C)) along N (C may be null: D = MXFP8(0)).  The K == 0 GEMM.
 cudaError_t launch_mxfp8_requantize(const uint8_t* c_data, const uint8_t* c_scales, uint8_t* d_data,
                                     uint8_t* d_scales, int64_t M, int64_t N, cudaStream_t stream);
@@ -24,6 +27,14 @@ cudaError_t launch_mxfp8_requantize(const uint8_t* c_data, const uint8_t* c_scal
 int launch_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const void* B,
                            const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                            uint8_t* D_scales, int M, int N, int K, cudaStream_t stream);
+
+// GEMM with the A operand dequantized to BF16 into `workspace` (gemm_workspace_bytes)
+// by a pre-pass, then streamed by TMA.
+size_t gemm_workspace_bytes(int M, int K);
+int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scales, const void* B,
+                                   const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
+                                   uint8_t* D_scales, int M, int N, int K, void* workspace,
+                                   cudaStream_t stream);
 
 // Device-side status word of the GEMM kernels (gemm.cu): read and clear.
 int read_and_clear_device_status(int* value);

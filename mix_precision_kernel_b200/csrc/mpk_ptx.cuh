@@ -375,6 +375,18 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar)
                  :: "r"(bar) : "memory");
 }
 
+// Per-warpgroup register reallocation (all 128 threads of the warpgroup execute it).
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec()
+{
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc()
+{
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" :: "n"(N));
+}
+
 // Named barrier over a subset of warps.
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads)
 {

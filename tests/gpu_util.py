@@ -23,8 +23,11 @@ def to_host(t) -> np.ndarray:
     return t.numpy()
 
 
-def run_gemm(mpk, inp: dict, device="cuda", with_c: bool = True, stream=None):
-    """D = A*B + C through mpk_gemm_mxfp8_bf16; returns (D_data, D_scales) on the host."""
+def run_gemm(mpk, inp: dict, device="cuda", with_c: bool = True, stream=None, path="default"):
+    """D = A*B + C; returns (D_data, D_scales) on the host.  path: "default"
+    (mpk_gemm_mxfp8_bf16, pooled workspace), "workspace" (mpk_gemm_mxfp8_bf16_ws
+    with a fresh caller workspace) or "onchip" (mpk_gemm_mxfp8_bf16_ws with no
+    workspace: A converted inside the GEMM kernel)."""
     import torch
 
     M, N, K = inp["M"], inp["N"], inp["K"]
@@ -37,7 +40,15 @@ def run_gemm(mpk, inp: dict, device="cuda", with_c: bool = True, stream=None):
         Cs = to_dev(inp["C_scales"], device)
     D = torch.full((M, N), 0xEE, dtype=torch.uint8, device=device)
     Ds = torch.full((M, (N + 31) // 32), 0xEE, dtype=torch.uint8, device=device)
-    mpk.gemm_fp8_tensorcore(A, As, B, C, Cs, D, Ds, M, N, K, stream)
+    if path == "workspace":
+        ws = torch.full((max(mpk.gemm_workspace_size(M, N, K), 16),), 0xEE, dtype=torch.uint8,
+                        device=device)
+        mpk.gemm_fp8_tensorcore_ws(A, As, B, C, Cs, D, Ds, M, N, K, ws, stream)
+    elif path == "onchip":
+        mpk.gemm_fp8_tensorcore_ws(A, As, B, C, Cs, D, Ds, M, N, K, None, stream)
+    else:
+        assert path == "default"
+        mpk.gemm_fp8_tensorcore(A, As, B, C, Cs, D, Ds, M, N, K, stream)
     torch.cuda.synchronize()
     return to_host(D), to_host(Ds)
 

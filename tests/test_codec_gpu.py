@@ -170,3 +170,39 @@ def test_full_size_against_oracle_and_value_idempotence(mpk_lib, cuda):
     assert same_f32(to_host(y), O.dequantize(d0, s0))
     del y, d, s
     torch.cuda.empty_cache()
+
+
+# ------------------------------ MXFP8 -> BF16 ------------------------------
+
+def _bf16_expected(d, s):
+    """Oracle dequantization rounded to BF16 (RNE); NaN positions returned apart."""
+    f = O.dequantize(d, s)
+    return O.to_bf16_bits(f), np.isnan(f)
+
+
+def _gpu_dequantize_bf16(mpk, d, s, offset=0):
+    import torch
+
+    M, K = d.shape
+    out = torch.full((M * K + offset,), 0x5555, dtype=torch.int16, device="cuda")
+    view = out[offset:]
+    mpk.mxfp8_dequantize_bf16_gpu(to_dev(d), to_dev(s), view.data_ptr(), M, K)
+    torch.cuda.synchronize()
+    return to_host(view).view(np.uint16).reshape(M, K)
+
+
+@pytest.mark.parametrize("M,K,offset", [(256, 256, 0), (37, 96, 0), (64, 100, 0), (33, 64, 3)])
+def test_dequantize_bf16_all_codes_all_scales(mpk_lib, cuda, M, K, offset):
+    """Every code under every scale byte: BF16 bits equal the oracle's value
+    rounded to nearest even (exact for scale >= 3), NaN exactly where the oracle
+    has NaN.  K % 32 != 0 or an unaligned output takes the element-wise kernel."""
+    rng = np.random.default_rng(M * K + offset)
+    d = (np.arange(M * K) % 256).astype(np.uint8).reshape(M, K)
+    rng.shuffle(d, axis=1)
+    s = rng.integers(0, 256, (M, (K + 31) // 32), dtype=np.uint8)
+    s.ravel()[:256] = np.arange(256, dtype=np.uint8)[: s.size]
+    got = _gpu_dequantize_bf16(mpk_lib, d, s, offset)
+    want, nan = _bf16_expected(d, s)
+    got_nan = ((got & 0x7F80) == 0x7F80) & ((got & 0x7F) != 0)
+    assert np.array_equal(nan, got_nan)
+    assert np.array_equal(got[~nan], want[~nan])

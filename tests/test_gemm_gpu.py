@@ -194,8 +194,11 @@ def test_invalid_arguments(mpk_lib, cuda):
 
 
 def test_stream_graph_capture_and_determinism(mpk_lib, cuda):
-    """The launch path allocates nothing and never synchronizes: it captures into
-    a CUDA graph on a side stream, and replays give bit-identical results."""
+    """No launch path synchronizes, so both entry points capture into a CUDA
+    graph on a side stream.  Under capture the default entry point takes the
+    on-chip conversion kernel (no workspace to allocate); the workspace entry
+    point captures the pre-pass with the caller's buffer.  Replays give results
+    bit-identical to the eager (pooled pre-pass) call."""
     import torch
 
     M, N, K = 512, 768, 512
@@ -221,6 +224,17 @@ def test_stream_graph_capture_and_determinism(mpk_lib, cuda):
         torch.cuda.synchronize()
         assert np.array_equal(to_host(D), eager_d) and np.array_equal(to_host(S), eager_s)
     del g
+    ws = torch.empty((mpk_lib.gemm_workspace_size(M, N, K),), dtype=torch.uint8, device="cuda")
+    g2 = torch.cuda.CUDAGraph()
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g2, stream=s):
+        mpk_lib.gemm_fp8_tensorcore_ws(A, As, B, C, Cs, D, S, M, N, K, ws, s)
+    for _ in range(2):
+        D.zero_(); S.zero_()
+        g2.replay()
+        torch.cuda.synchronize()
+        assert np.array_equal(to_host(D), eager_d) and np.array_equal(to_host(S), eager_s)
+    del g2
 
 
 def test_wait_timeout_reports_status_without_fault(mpk_lib, cuda):

@@ -1,0 +1,124 @@
+"""The three GEMM paths give the same D, bit for bit:
+
+- mpk_gemm_mxfp8_bf16: A dequantized exactly to BF16 by a bandwidth pre-pass
+  into a pooled workspace, then the TMA-fed BF16 x BF16 tensor-core kernel;
+- mpk_gemm_mxfp8_bf16_ws with a caller workspace: the same kernels;
+- mpk_gemm_mxfp8_bf16_ws with no workspace: A converted to BF16 on chip by the
+  GEMM kernel's own transform warps.
+
+All feed the same BF16 values to the same MMA sequence, so each meets the parity
+bar against the oracle that the default path is held to."""
+import numpy as np
+import pytest
+
+import oracle as O
+from gpu_util import run_gemm, to_dev, to_host
+from test_gemm_gpu import check_parity
+
+pytestmark = pytest.mark.gpu
+
+
+def _both(mpk_lib, inp, with_c=True):
+    d0, s0 = run_gemm(mpk_lib, inp, with_c=with_c)
+    for path in ("workspace", "onchip"):
+        d1, s1 = run_gemm(mpk_lib, inp, with_c=with_c, path=path)
+        assert np.array_equal(d0, d1) and np.array_equal(s0, s1), path
+    return d0, s0
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (512, 512, 512), (256, 512, 1024),
+                                   (1024, 1024, 1024)])
+def test_ws_reference_shapes(mpk_lib, cuda, M, N, K):
+    inp = O.make_gemm_inputs(M, N, K, seed=42)
+    Dd, Ds = _both(mpk_lib, inp)
+    check_parity(Dd, Ds, O.gold_mx(inp), f"ws {M}x{N}x{K}")
+
+
+@pytest.mark.parametrize("M,N,K", [(200, 264, 80), (130, 136, 48), (1, 8, 16), (129, 520, 1104),
+                                   (64, 2056, 192), (384, 256, 4112)])
+@pytest.mark.parametrize("with_c", [True, False])
+def test_ws_ragged(mpk_lib, cuda, M, N, K, with_c):
+    """K % 32 != 0 takes the element-wise pre-pass; ragged M/N/K tiles are
+    zero-filled by TMA."""
+    inp = O.make_gemm_inputs(M, N, K, seed=M + N + K, with_c=with_c)
+    Dd, Ds = _both(mpk_lib, inp, with_c=with_c)
+    check_parity(Dd, Ds, O.gold_mx(inp), f"ws ragged {M}x{N}x{K} C={with_c}")
+
+
+@pytest.mark.parametrize("with_nan", [False, True])
+def test_ws_exotic_scales_and_nan_codes(mpk_lib, cuda, with_nan):
+    """Scale bytes 0-2, 134/135 and 247-255 and NaN codes take the pre-pass's
+    general conversion; results equal the fused kernel's."""
+    M, N, K = 256, 256, 256
+    inp = O.make_gemm_inputs(M, N, K, seed=78)
+    rng = np.random.default_rng(78)
+    pool = np.array([0, 1, 2, 3, 114, 134, 135, 200, 246, 247, 254, 255], np.uint8)
+    sc = inp["A_scales"].copy()
+    rows = rng.choice(M, 48, replace=False)
+    sc[rows] = rng.choice(pool, (48, sc.shape[1]))
+    inp["A_scales"] = sc
+    if with_nan:
+        d = inp["A_data"].copy()
+        idx = rng.choice(M * K, 20, replace=False)
+        d.ravel()[idx] = rng.choice(np.array([0x7F, 0xFF], np.uint8), 20)
+        inp["A_data"] = d
+    inp["A_deq"] = O.dequantize(inp["A_data"], inp["A_scales"])
+    Dd, Ds = _both(mpk_lib, inp)
+    gold = O.gold_mx(inp)
+    hist = O.mx_ulp_hist(Dd, Ds, gold[1], gold[2])
+    assert hist[3] == 0
+    assert hist[0] + hist[1] >= 0.999 * sum(hist)
+
+
+def test_ws_prepass_is_exact_bf16(mpk_lib, cuda):
+    """The workspace holds code x 2^(s-127) rounded to BF16 (exact for s >= 3)."""
+    import torch
+
+    M, N, K = 96, 64, 256
+    inp = O.make_gemm_inputs(M, N, K, seed=5)
+    rng = np.random.default_rng(5)
+    inp["A_scales"] = rng.integers(0, 256, inp["A_scales"].shape, dtype=np.uint8)
+    A, As, B = to_dev(inp["A_data"]), to_dev(inp["A_scales"]), to_dev(inp["B_bf16"])
+    D = torch.empty((M, N), dtype=torch.uint8, device="cuda")
+    Ds = torch.empty((M, N // 32), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros((mpk_lib.gemm_workspace_size(M, N, K),), dtype=torch.uint8, device="cuda")
+    mpk_lib.gemm_fp8_tensorcore_ws(A, As, B, None, None, D, Ds, M, N, K, ws)
+    torch.cuda.synchronize()
+    got = to_host(ws).view(np.uint16).reshape(M, K)
+    want = O.to_bf16_bits(O.dequantize(inp["A_data"], inp["A_scales"]))
+    nan = np.isnan(O.dequantize(inp["A_data"], inp["A_scales"]))
+    got_nan = ((got & 0x7F80) == 0x7F80) & ((got & 0x7F) != 0)
+    assert np.array_equal(nan, got_nan)
+    assert np.array_equal(got[~nan], want[~nan])
+
+
+def test_ws_argument_checks(mpk_lib, cuda):
+    import torch
+
+    M, N, K = 128, 128, 128
+    inp = O.make_gemm_inputs(M, N, K, seed=1)
+    A, As, B = to_dev(inp["A_data"]), to_dev(inp["A_scales"]), to_dev(inp["B_bf16"])
+    D = torch.empty((M, N), dtype=torch.uint8, device="cuda")
+    Ds = torch.empty((M, N // 32), dtype=torch.uint8, device="cuda")
+    need = mpk_lib.gemm_workspace_size(M, N, K)
+    assert need == M * K * 2
+    small = torch.empty((need - 16,), dtype=torch.uint8, device="cuda")
+    with pytest.raises(mpk_lib.MpkError) as e:
+        mpk_lib.gemm_fp8_tensorcore_ws(A, As, B, None, None, D, Ds, M, N, K, small)
+    assert e.value.status == mpk_lib.MPK_ERR_INVALID_VALUE
+    big = torch.empty((need + 32,), dtype=torch.uint8, device="cuda")
+    with pytest.raises(mpk_lib.MpkError) as e:
+        mpk_lib.gemm_fp8_tensorcore_ws(A, As, B, None, None, D, Ds, M, N, K, big[8:].data_ptr())
+    assert e.value.status == mpk_lib.MPK_ERR_MISALIGNED
+
+
+def test_pool_release_and_reuse(mpk_lib, cuda):
+    """The pooled workspace can be handed back between calls; later calls take a
+    fresh one and give the same D."""
+    inp = O.make_gemm_inputs(256, 512, 512, seed=3)
+    d0, s0 = run_gemm(mpk_lib, inp)
+    mpk_lib.release_workspace_pool()
+    d1, s1 = run_gemm(mpk_lib, inp)
+    mpk_lib.release_workspace_pool()
+    mpk_lib.release_workspace_pool()
+    assert np.array_equal(d0, d1) and np.array_equal(s0, s1)
