@@ -76,6 +76,26 @@ int mpk_gemm_workspace_size(int M, int N, int K, size_t* bytes);
  * work queued on it has finished.  No counterpart in the reference. */
 int mpk_release_workspace_pool(void);
 
+/* Fixed size of the device array behind mpk_gemm_mxfp8_bf16_noalloc: 32 MiB per
+ * device, enough for the BF16 copy of an A with M*K <= 16,777,216 (4096 x 4096). */
+#define MPK_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
+/* Same computation as mpk_gemm_mxfp8_bf16, for callers that may not allocate
+ * device memory once running (a caching allocator that has reserved the device, a
+ * latency-bound loop, a fixed memory budget).  The A workspace is a fixed array in
+ * the library's device image (MPK_NOALLOC_SCRATCH_BYTES per device, held from
+ * the image's load); this call allocates nothing.  Sizes with M*K*2 above that
+ * return MPK_ERR_UNSUPPORTED.  Nothing in the array needs to start at zero.
+ * All calls on a device share the array: calls that can run at the same time
+ * (different streams without an event between them, or unordered host threads)
+ * race, so issue them on one stream or order them.  The first call on each device
+ * looks up the array's address; if that first call would be made inside a stream
+ * capture, make one call before the capture instead.  No counterpart in the
+ * reference. */
+int mpk_gemm_mxfp8_bf16_noalloc(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
+                                const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
+                                uint8_t* D_scales, int M, int N, int K, void* stream);
+
 /* float [M][K] -> MXFP8 along K.  Replaces mxfp8_quantize_gpu (reference
  * include/mxfp8_utils.h:38-40, src/quantize/mxfp8_quantize.cu:82-88).  Bit-exact
  * with the reference's host and device quantizers.  Any K >= 1. */

@@ -27,7 +27,7 @@ __all__ = [
     "gemm_fp8_tensorcore", "mxfp8_quantize_gpu", "mxfp8_dequantize_gpu",
     "mxfp8_quantize_host", "mxfp8_dequantize_host",
     "gemm_fp8_tensorcore_ws", "gemm_workspace_size", "release_workspace_pool",
-    "mxfp8_dequantize_bf16_gpu",
+    "mxfp8_dequantize_bf16_gpu", "gemm_fp8_tensorcore_noalloc", "NOALLOC_SCRATCH_BYTES",
     "gemm", "quantize", "dequantize", "device_status", "set_wait_timeout_ns", "wait_selftest",
     "MX_BLOCK", "nblk",
 ]
@@ -76,6 +76,7 @@ def lib() -> ctypes.CDLL:
                                                  ctypes.c_size_t, vp]
             L.mpk_gemm_workspace_size.argtypes = [ci, ci, ci, ctypes.POINTER(ctypes.c_size_t)]
             L.mpk_release_workspace_pool.argtypes = []
+            L.mpk_gemm_mxfp8_bf16_noalloc.argtypes = [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, vp]
             L.mpk_mxfp8_quantize.argtypes = [vp, vp, vp, ci, ci, vp]
             L.mpk_mxfp8_dequantize.argtypes = [vp, vp, vp, ci, ci, vp]
             L.mpk_mxfp8_dequantize_bf16.argtypes = [vp, vp, vp, ci, ci, vp]
@@ -90,7 +91,7 @@ def lib() -> ctypes.CDLL:
             L.mpk_last_error.restype = ctypes.c_char_p
             for f in ("mpk_gemm_mxfp8_bf16", "mpk_gemm_mxfp8_bf16_ws", "mpk_gemm_workspace_size",
                       "mpk_release_workspace_pool", "mpk_mxfp8_quantize", "mpk_mxfp8_dequantize",
-                      "mpk_mxfp8_dequantize_bf16",
+                      "mpk_mxfp8_dequantize_bf16", "mpk_gemm_mxfp8_bf16_noalloc",
                       "mpk_mxfp8_quantize_host", "mpk_mxfp8_dequantize_host", "mpk_device_status",
                       "mpk_set_wait_timeout_ns", "mpk_wait_selftest", "mpk_version"):
                 getattr(L, f).restype = ci
@@ -166,6 +167,20 @@ def gemm_fp8_tensorcore_ws(A_data, A_scales, B, C_data, C_scales, D_data, D_scal
     _check(lib().mpk_gemm_mxfp8_bf16_ws(_addr(A_data), _addr(A_scales), _addr(B), _addr(C_data),
                                         _addr(C_scales), _addr(D_data), _addr(D_scales), M, N, K,
                                         _addr(workspace), nbytes, s))
+
+
+NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024  # MPK_NOALLOC_SCRATCH_BYTES in include/mpk.h
+
+
+def gemm_fp8_tensorcore_noalloc(A_data, A_scales, B, C_data, C_scales, D_data, D_scales,
+                                M: int, N: int, K: int, stream=None) -> None:
+    """gemm_fp8_tensorcore for callers that may not allocate device memory: the A
+    workspace is the library's fixed per-device array (M*K*2 <= NOALLOC_SCRATCH_BYTES).
+    Calls that can overlap on one device share that array and race; issue them on
+    one stream or order them."""
+    s = _stream(stream, A_data, D_data)
+    _check(lib().mpk_gemm_mxfp8_bf16_noalloc(_addr(A_data), _addr(A_scales), _addr(B), _addr(C_data),
+                                             _addr(C_scales), _addr(D_data), _addr(D_scales), M, N, K, s))
 
 
 def release_workspace_pool() -> None:

@@ -407,3 +407,83 @@ int mpk_wait_selftest(uint64_t timeout_ns, void* stream)
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free GEMM: mpk_gemm_mxfp8_bf16_noalloc
+// ---------------------------------------------------------------------------
+// Who needs it: callers that may not allocate device memory once they are running.
+// A serving loop whose framework's caching allocator has reserved (nearly) all of
+// HBM at start-up would see a driver or pool allocation fail or fragment memory it
+// does not own; a latency-bound loop cannot afford the first-use cost of growing a
+// pool (an OS mapping of new device memory) in the middle of a request; a process
+// running under a fixed device-memory budget must know its footprint before its
+// first request.  For them this entry point runs the same two kernels as
+// mpk_gemm_mxfp8_bf16 (A pre-pass, then the tensor-core kernel) with the BF16 copy
+// of A in the fixed array below, which is part of the library's device image: it
+// takes MPK_NOALLOC_SCRATCH_BYTES of device memory on each device from the moment
+// the image is loaded there, and the call path itself allocates nothing.
+//
+// Contents: nothing in the array has to start at zero or hold anything between
+// calls.  Each call's pre-pass writes all M*K*2 bytes that the call's GEMM kernel
+// then reads (rows and columns outside M x K are never read; the tensor-map loads
+// fill them with zeros).
+//
+// Ordering: one array per device, shared by every call on that device.  Two calls
+// whose kernels can be in flight at the same time (different streams without an
+// event between them, or different host threads without ordering) race: one call's
+// pre-pass can overwrite A while the other's GEMM reads it.  Issue the calls on one
+// stream, or order them with events.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[MPK_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+}  // namespace
+
+// Device address of g_noalloc_scratch on the current device, looked up once per
+// device (with that device current) and cached.
+static int noalloc_scratch(void** out)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return from_cuda(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) {
+        set_last_error("device ordinal %d out of range", dev);
+        return MPK_ERR_INVALID_VALUE;
+    }
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess) return from_cuda(e, "cudaGetSymbolAddress of the no-alloc scratch");
+        g_noalloc_addr[dev] = ptr;
+    }
+    *out = g_noalloc_addr[dev];
+    return MPK_SUCCESS;
+}
+
+extern "C" int mpk_gemm_mxfp8_bf16_noalloc(const uint8_t* A_data, const uint8_t* A_scales,
+                                           const void* B_bf16, const uint8_t* C_data,
+                                           const uint8_t* C_scales, uint8_t* D_data,
+                                           uint8_t* D_scales, int M, int N, int K, void* stream)
+{
+    bool done = false;
+    if (int rc = validate_gemm(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales, M, N, K, done))
+        return rc;
+    if (done) return MPK_SUCCESS;
+    const cudaStream_t st = (cudaStream_t)stream;
+    if (K == 0)
+        return from_cuda(launch_mxfp8_requantize(C_data, C_scales, D_data, D_scales, M, N, st),
+                         "requantize launch");
+    const size_t need = gemm_workspace_bytes(M, K);
+    if (need > (size_t)MPK_NOALLOC_SCRATCH_BYTES) {
+        set_last_error("mpk_gemm_mxfp8_bf16_noalloc: M*K*2 = %zu bytes exceeds its fixed scratch of %zu "
+                       "bytes (M*K <= %zu); use mpk_gemm_mxfp8_bf16 or mpk_gemm_mxfp8_bf16_ws",
+                       need, (size_t)MPK_NOALLOC_SCRATCH_BYTES, (size_t)MPK_NOALLOC_SCRATCH_BYTES / 2);
+        return MPK_ERR_UNSUPPORTED;
+    }
+    void* scratch = nullptr;
+    if (int rc = noalloc_scratch(&scratch)) return rc;
+    return launch_gemm_mxfp8_bf16_prepass(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales,
+                                          M, N, K, scratch, st);
+}
