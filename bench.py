@@ -465,7 +465,10 @@ def run_reference_arm(args, world, rank):
     if rank != 0:
         return None
     M, N, K, seed = WORKLOADS.get(args.workload, WORKLOADS["dense_projection"])
+    # Each step is a bounded row sample; the per-step budget shrinks with the step
+    # count so that the whole run stays within about two minutes of host work.
     budget = float(os.environ.get("MPK_REF_STEP_BUDGET_S", "2.0"))
+    budget = max(0.05, min(budget, 120.0 / (args.steps + args.warmup)))
     vals = []
     desc = None
     for i in range(args.warmup + args.steps):
