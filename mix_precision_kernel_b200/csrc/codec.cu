@@ -6,12 +6,12 @@
 //
 // Both directions are bit-exact against the reference's host functions.
 //
-// Fast path (K % 32 == 0, 16-byte aligned pointers): the tensor is a flat run of
-// 32-element blocks whose scale index equals the flat block index, so a warp
-// streams 1 KiB of FP32 (quantize) or 256 B of codes (dequantize) per step with
-// fully coalesced 16-byte accesses.  Four lanes own one block (8 elements each);
-// the block amax is a two-step xor shuffle.  General path (ragged K, e.g.
-// K = 100, or unaligned pointers): one warp per (row, block), one element per lane.
+// Fast path (K % 32 == 0, aligned pointers): the tensor is a flat run of 32-element
+// blocks whose scale index equals the flat block index.  Each warp instruction
+// touches one contiguous span (512 B of FP32, 128 B of codes), lanes issue several
+// loads before any arithmetic, and the grid covers every SM with 2048 threads.
+// General path (ragged K, e.g. K = 100, or unaligned pointers): one warp per
+// (row, block), one element per lane.
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <cuda_bf16.h>
@@ -25,38 +25,50 @@ constexpr int kCodecThreads = 256;
 
 // ------------------------------- quantize ----------------------------------
 
+// Flat quantize: lane l of a warp holds float4 number base + 32j + l for j < kQuantU,
+// so every load instruction reads 512 contiguous bytes and every code store writes
+// 128; an MX block (8 float4) sits in 8 consecutive lanes, whose amax is three
+// xor-shuffles.  kQuantU loads are issued before any arithmetic (64 B in flight per
+// thread).
+constexpr int kQuantU = 4;
+
 __global__ void __launch_bounds__(kCodecThreads)
 mxfp8_quantize_flat_kernel(const float* __restrict__ in, uint8_t* __restrict__ data,
-                           uint8_t* __restrict__ scales, int64_t n_quarters)
+                           uint8_t* __restrict__ scales, int64_t n_f4)
 {
     const int lane = threadIdx.x & 31;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    // The trip count is warp-uniform (q - lane is the same for the whole warp and
-    // the stride is a multiple of 32), so the full-mask shuffles below are legal;
-    // lanes past the end compute on zeros and store nothing.
-    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q - lane < n_quarters;
-         q += stride) {
-        const bool valid = q < n_quarters;
-        float v[8];
-        if (valid) {
-            const float4* p = reinterpret_cast<const float4*>(in) + 2 * q;
-            float4 a = __ldcs(p), b = __ldcs(p + 1);
-            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-            v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-        } else {
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const float4* i4 = reinterpret_cast<const float4*>(in);
+    uint32_t* d32 = reinterpret_cast<uint32_t*>(data);
+    // base is warp-uniform, so the full-mask shuffles are legal; lanes past the end
+    // compute on zeros and store nothing.
+    for (int64_t base = warp * 32 * kQuantU; base < n_f4; base += nwarps * 32 * kQuantU) {
+        float4 v[kQuantU];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+        for (int j = 0; j < kQuantU; ++j) {
+            const int64_t f = base + 32 * j + lane;
+            v[j] = f < n_f4 ? __ldcs(i4 + f) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
-        float amax = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));  // NaN ignored
-        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
-        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
-        float inv;
-        const uint32_t s = mx_block_scale(amax, inv);
-        if (valid) {
-            __stcs(reinterpret_cast<uint2*>(data) + q, quantize8(v, inv));
-            if ((q & 3) == 0) scales[q >> 2] = (uint8_t)s;
+        for (int j = 0; j < kQuantU; ++j) {
+            const int64_t f = base + 32 * j + lane;
+            // The reference folds its max from 0 (src/quantize/mxfp8_quantize.cu:125-128), so
+            // NaN elements are ignored and an all-NaN block has amax 0: the final
+            // fmaxf with 0 turns the tree's NaN (every operand NaN) into that 0.
+            float amax = fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w)));
+            amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+            amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));
+            amax = fmaxf(amax, 0.0f);
+            float inv;
+            const uint32_t s = mx_block_scale(amax, inv);
+            if (f < n_f4) {
+                const uint32_t c0 = f32x2_to_e4m3x2(v[j].x * inv, v[j].y * inv);
+                const uint32_t c1 = f32x2_to_e4m3x2(v[j].z * inv, v[j].w * inv);
+                __stcs(d32 + f, c0 | (c1 << 16));
+                if ((lane & 7) == 0) scales[f >> 3] = (uint8_t)s;
+            }
         }
     }
 }
@@ -110,19 +122,37 @@ mxfp8_requantize_kernel(const uint8_t* __restrict__ c_data, const uint8_t* __res
 
 // ------------------------------ dequantize ---------------------------------
 
+// Flat dequantize: lane l of a warp converts code quad base + 32j + l for j <
+// kDequantU, so every code load reads 128 contiguous bytes and every float4 store
+// writes 512; the kDequantU loads are issued first.
+constexpr int kDequantU = 8;
+
 __global__ void __launch_bounds__(kCodecThreads)
 mxfp8_dequantize_flat_kernel(const uint8_t* __restrict__ data, const uint8_t* __restrict__ scales,
-                             float* __restrict__ out, int64_t n_octets)
+                             float* __restrict__ out, int64_t n_quads)
 {
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < n_octets; o += stride) {
-        const uint2 c = __ldcs(reinterpret_cast<const uint2*>(data) + o);
-        const float s = e8m0_to_f32(__ldg(scales + (o >> 2)));
-        float2 f0 = e4m3x2_to_f32x2(c.x), f1 = e4m3x2_to_f32x2(c.x >> 16);
-        float2 f2 = e4m3x2_to_f32x2(c.y), f3 = e4m3x2_to_f32x2(c.y >> 16);
-        float4* p = reinterpret_cast<float4*>(out) + 2 * o;
-        __stcs(p, make_float4(f0.x * s, f0.y * s, f1.x * s, f1.y * s));
-        __stcs(p + 1, make_float4(f2.x * s, f2.y * s, f3.x * s, f3.y * s));
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const uint32_t* d32 = reinterpret_cast<const uint32_t*>(data);
+    float4* o4 = reinterpret_cast<float4*>(out);
+    for (int64_t base = warp * 32 * kDequantU; base < n_quads; base += nwarps * 32 * kDequantU) {
+        uint32_t c[kDequantU], sb[kDequantU];
+#pragma unroll
+        for (int j = 0; j < kDequantU; ++j) {
+            const int64_t q = base + 32 * j + lane;
+            c[j] = q < n_quads ? __ldcs(d32 + q) : 0u;
+            sb[j] = q < n_quads ? __ldg(scales + (q >> 3)) : 0u;
+        }
+#pragma unroll
+        for (int j = 0; j < kDequantU; ++j) {
+            const int64_t q = base + 32 * j + lane;
+            if (q < n_quads) {
+                const float sc = e8m0_to_f32(sb[j]);
+                const float2 a = e4m3x2_to_f32x2(c[j]), b = e4m3x2_to_f32x2(c[j] >> 16);
+                __stcs(o4 + q, make_float4(a.x * sc, a.y * sc, b.x * sc, b.y * sc));
+            }
+        }
     }
 }
 
@@ -198,15 +228,32 @@ __device__ __forceinline__ uint4 e4m3x8_to_bf16x8(uint2 c, uint32_t s)
 }
 
 // K % 32 == 0, 8-byte aligned codes, 16-byte aligned output: flat run of blocks.
+// Lane l of a warp converts octet base + 32j + l for j < kPrepassU (loads first).
+// The BF16 output is stored with the default policy so that it stays in L2 for
+// the GEMM that reads it next.
+constexpr int kPrepassU = 2;
+
 __global__ void __launch_bounds__(kCodecThreads)
 mxfp8_dequantize_bf16_flat_kernel(const uint8_t* __restrict__ data, const uint8_t* __restrict__ scales,
                                   uint16_t* __restrict__ out, int64_t n_octets)
 {
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < n_octets; o += stride) {
-        const uint2 c = __ldcs(reinterpret_cast<const uint2*>(data) + o);
-        const uint32_t s = __ldg(scales + (o >> 2));
-        reinterpret_cast<uint4*>(out)[o] = e4m3x8_to_bf16x8(c, s);
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t base = warp * 32 * kPrepassU; base < n_octets; base += nwarps * 32 * kPrepassU) {
+        uint2 c[kPrepassU];
+        uint32_t sb[kPrepassU];
+#pragma unroll
+        for (int j = 0; j < kPrepassU; ++j) {
+            const int64_t o = base + 32 * j + lane;
+            c[j] = o < n_octets ? __ldcs(reinterpret_cast<const uint2*>(data) + o) : make_uint2(0u, 0u);
+            sb[j] = o < n_octets ? __ldg(scales + (o >> 2)) : 127u;
+        }
+#pragma unroll
+        for (int j = 0; j < kPrepassU; ++j) {
+            const int64_t o = base + 32 * j + lane;
+            if (o < n_octets) reinterpret_cast<uint4*>(out)[o] = e4m3x8_to_bf16x8(c[j], sb[j]);
+        }
     }
 }
 
@@ -242,9 +289,10 @@ cudaError_t launch_mxfp8_quantize(const float* in, uint8_t* data, uint8_t* scale
 {
     const int64_t nblk = (K + 31) / 32;
     if (M == 0 || K == 0) return cudaSuccess;
-    if (K % 32 == 0 && aligned16(in) && (reinterpret_cast<uintptr_t>(data) & 7u) == 0) {
-        const int64_t nq = M * K / 8;
-        mxfp8_quantize_flat_kernel<<<codec_grid(nq), kCodecThreads, 0, stream>>>(in, data, scales, nq);
+    if (K % 32 == 0 && aligned16(in) && (reinterpret_cast<uintptr_t>(data) & 3u) == 0) {
+        const int64_t nf4 = M * K / 4;
+        mxfp8_quantize_flat_kernel<<<codec_grid(nf4 / kQuantU), kCodecThreads, 0, stream>>>(in, data, scales,
+                                                                                         nf4);
     } else {
         mxfp8_quantize_rowblock_kernel<<<codec_grid(M * nblk * 32), kCodecThreads, 0, stream>>>(
             in, data, scales, M, K, nblk);
@@ -257,9 +305,10 @@ cudaError_t launch_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, 
 {
     const int64_t nblk = (K + 31) / 32;
     if (M == 0 || K == 0) return cudaSuccess;
-    if (K % 32 == 0 && aligned16(out) && (reinterpret_cast<uintptr_t>(data) & 7u) == 0) {
-        const int64_t no = M * K / 8;
-        mxfp8_dequantize_flat_kernel<<<codec_grid(no), kCodecThreads, 0, stream>>>(data, scales, out, no);
+    if (K % 32 == 0 && aligned16(out) && (reinterpret_cast<uintptr_t>(data) & 3u) == 0) {
+        const int64_t nq = M * K / 4;
+        mxfp8_dequantize_flat_kernel<<<codec_grid(nq / kDequantU), kCodecThreads, 0, stream>>>(data, scales,
+                                                                                            out, nq);
     } else {
         mxfp8_dequantize_elem_kernel<<<codec_grid(M * K), kCodecThreads, 0, stream>>>(
             data, scales, out, M, K, nblk);
@@ -275,7 +324,8 @@ cudaError_t launch_mxfp8_dequantize_bf16(const uint8_t* data, const uint8_t* sca
     uint16_t* o = static_cast<uint16_t*>(out);
     if (K % 32 == 0 && aligned16(out) && (reinterpret_cast<uintptr_t>(data) & 7u) == 0) {
         const int64_t no = M * K / 8;
-        mxfp8_dequantize_bf16_flat_kernel<<<codec_grid(no), kCodecThreads, 0, stream>>>(data, scales, o, no);
+        mxfp8_dequantize_bf16_flat_kernel<<<codec_grid(no / kPrepassU), kCodecThreads, 0, stream>>>(
+            data, scales, o, no);
     } else {
         mxfp8_dequantize_bf16_elem_kernel<<<codec_grid(M * K), kCodecThreads, 0, stream>>>(
             data, scales, o, M, K, nblk);

@@ -18,19 +18,7 @@ namespace mpk {
 //   include/fp8_types.h:8-12     E4M3 -> float, exact
 //   include/fp8_types.h:14-21    float -> E4M3: NaN -> 0x7F, clamp +-448, RNE
 // ---------------------------------------------------------------------------
-constexpr float kE4M3Max = 448.0f;
-constexpr float kScaleFloor = 1.1754944e-38f;  // src/quantize/mxfp8_quantize.cu:131
-
 __device__ __forceinline__ float e8m0_to_f32(uint32_t b) { return __uint_as_float(b << 23); }
-
-__device__ __forceinline__ uint32_t f32_to_e8m0_roundup(float x)
-{
-    if (x <= 0.0f) return 0u;
-    uint32_t bits = __float_as_uint(x);
-    uint32_t e = (bits >> 23) & 0xFFu;
-    if (bits & 0x007FFFFFu) e = (e < 255u) ? e + 1u : 255u;
-    return e;
-}
 
 // Two E4M3 codes (low byte = first element) -> two floats, exact.
 __device__ __forceinline__ float2 e4m3x2_to_f32x2(uint32_t two_codes)
@@ -44,31 +32,45 @@ __device__ __forceinline__ float2 e4m3x2_to_f32x2(uint32_t two_codes)
     return make_float2(lo, hi);
 }
 
-// Clamp to +-448 and round to nearest even into E4M3; NaN -> 0x7F.
+// The reference's clamp to +-448 followed by round-to-nearest-even into E4M3,
+// with NaN -> 0x7F (include/fp8_types.h:14-21).  cvt.rn.satfinite saturates
+// out-of-range values and infinities to +-448 itself, so the explicit clamp is
+// not needed: with and without it the codes agree for every float bit pattern in
+// either slot (checked exhaustively on sm_100a).
 // Returns two codes packed as (second << 8) | first.
 __device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float first, float second)
 {
-    float a = fminf(fmaxf(first, -kE4M3Max), kE4M3Max);
-    float b = fminf(fmaxf(second, -kE4M3Max), kE4M3Max);
     uint32_t r;
     // cvt packs its first source into the upper byte.
     asm("{\n\t.reg .b16 c;\n\tcvt.rn.satfinite.e4m3x2.f32 c, %1, %2;\n\tcvt.u32.u16 %0, c;\n\t}"
-        : "=r"(r) : "f"(b), "f"(a));
+        : "=r"(r) : "f"(second), "f"(first));
     if (first != first) r = (r & 0xFF00u) | 0x7Fu;
     if (second != second) r = (r & 0x00FFu) | 0x7F00u;
     return r;
 }
 
 // Block scale for one MX block from its amax (src/quantize/mxfp8_quantize.cu:26-37):
-// returns the E8M0 byte and sets inv to 1/scale (0 when the scale is 0 or inf
-// maps to 0 through the division).
+// the reference takes q = amax / 448 rounded to nearest, clamps it below at
+// FLT_MIN, rounds it up to a power of two as an E8M0 byte s, and multiplies the
+// elements by 1 / 2^(s-127).  The same bits without a division:
+//   - 448 = 1.75 * 2^8 and the FP32 neighbours of 448 * 2^e lie further than half
+//     an ulp of 2^e from it after the division, so for a normal quotient q is a
+//     power of two exactly when amax = 448 * 2^e, and s = ceil(log2(amax / 448)) + 127
+//     = (exponent field of amax) - 8 + (mantissa field of amax > 0x600000);
+//   - quotients below FLT_MIN (amax < 448 * 2^-126, zero included) give s = 1;
+//   - amax = +inf gives s = 255, whose scale is inf and whose inverse is 0;
+//   - the inverse 2^(127-s) is exact: exponent field 254 - s, or the subnormal
+//     2^-127 for s = 254.
+// amax is never negative or NaN (fmaxf drops NaN).  This matches the division
+// rule for every non-negative float amax (checked exhaustively, all 2^31 + 1).
 __device__ __forceinline__ uint32_t mx_block_scale(float amax, float& inv)
 {
-    float scale_val = __fdiv_rn(amax, kE4M3Max);
-    if (scale_val < kScaleFloor) scale_val = kScaleFloor;
-    uint32_t s = f32_to_e8m0_roundup(scale_val);
-    float actual = e8m0_to_f32(s);
-    inv = (actual > 0.0f) ? __fdiv_rn(1.0f, actual) : 0.0f;
+    const uint32_t u = __float_as_uint(amax);
+    const int t = (int)(u >> 23) - 8 + ((u & 0x7FFFFFu) > 0x600000u ? 1 : 0);
+    uint32_t s = t < 1 ? 1u : (uint32_t)t;
+    if (u >= 0x7F800000u) s = 255u;
+    const uint32_t ib = s >= 255u ? 0u : (s == 254u ? 0x00400000u : (254u - s) << 23);
+    inv = __uint_as_float(ib);
     return s;
 }
 
