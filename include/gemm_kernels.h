@@ -20,10 +20,12 @@
 
 #include "mpk.h"
 
-// Same signature and argument meaning as the reference (include/gemm_kernels.h:12-16).
-// Differences: no per-call allocation or implicit device synchronization; any
-// failure (unsupported shape: K % 16 or N % 8 nonzero; misaligned A/B; no sm_100
-// device) prints a message and exits, as the reference's CUDA_CHECK does.
+// Same signature and argument meaning as the reference (include/gemm_kernels.h:12-16),
+// any M, N, K.  Differences: no per-call cudaMalloc/cudaFree or implicit device
+// synchronization (the A workspace comes from a pooled, stream-ordered reserve); any
+// failure (no sm_100 device, out of memory, a shape the on-chip kernel cannot take
+// while the stream is being captured) prints a message and exits, as the
+// reference's CUDA_CHECK does.
 inline void gemm_fp8_tensorcore(const uint8_t* d_A_data, const uint8_t* d_A_scales,
                                 const __nv_bfloat16* d_B, const uint8_t* d_C_data,
                                 const uint8_t* d_C_scales, uint8_t* d_D_data, uint8_t* d_D_scales,

@@ -38,38 +38,43 @@ extern "C" {
 enum {
     MPK_SUCCESS = 0,
     MPK_ERR_INVALID_VALUE = 1001,   /* null pointer, negative size, size overflow */
-    MPK_ERR_UNSUPPORTED = 1002,     /* shape/stride the kernel does not handle (see mpk_status_string) */
-    MPK_ERR_MISALIGNED = 1003,      /* pointer alignment required by TMA not met */
+    MPK_ERR_UNSUPPORTED = 1002,     /* shape or size an entry point does not handle (see mpk_last_error) */
+    MPK_ERR_MISALIGNED = 1003,      /* pointer alignment an entry point requires is not met */
     MPK_ERR_DEVICE_TIMEOUT = 1004,  /* a bounded device-side wait expired (read by mpk_device_status) */
     MPK_ERR_ARCH = 1005,            /* current device is not sm_100 */
     MPK_ERR_DRIVER = 1006           /* CUDA driver entry point or tensor-map encoding failed */
 };
 
 /* D = A*B + C.  Replaces gemm_fp8_tensorcore (reference include/gemm_kernels.h:12-16,
- * src/kernels/gemm_fp8_tensorcore.cu:231-249).  Requirements: K % 16 == 0 and
- * N % 8 == 0 (TMA row strides), A_data and B 16-byte aligned.  C_data/C_scales
- * may both be NULL (no C term).
+ * src/kernels/gemm_fp8_tensorcore.cu:231-249).  Any M, N, K >= 0 and any pointer
+ * alignment, as in the reference.  C_data/C_scales may both be NULL (no C term).
  *
  * A is dequantized exactly to BF16 by a bandwidth pre-pass into a workspace taken
- * from the library's pool on `stream`, then the tensor-core kernel streams both
- * operands by TMA.  While `stream` is being captured into a CUDA graph (or if the
- * pool cannot supply the workspace) the kernel that converts A on chip runs
- * instead; it needs no workspace and its D is bit-identical. */
+ * from the library's pool on `stream` (rows padded to a multiple of 8 elements; B is
+ * also copied there with padded rows when N % 8 != 0 or B is not 16-byte aligned),
+ * then the tensor-core kernel streams both operands by TMA.  While `stream` is
+ * being captured into a CUDA graph (or if the pool cannot supply the workspace) the
+ * kernel that converts A on chip runs instead: it needs no workspace and gives a
+ * bit-identical D, but needs K % 16 == 0, N % 8 == 0 and 16-byte aligned A_data and B
+ * (else MPK_ERR_UNSUPPORTED / MPK_ERR_MISALIGNED). */
 int mpk_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
                         const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                         uint8_t* D_scales, int M, int N, int K, void* stream);
 
-/* Same computation with a caller-provided workspace: at least
- * mpk_gemm_workspace_size() bytes (M*K*2), 16-byte aligned, not used by other
- * work in flight until this call's kernels have finished on `stream`.  With
- * workspace == NULL the on-chip conversion kernel runs (no workspace at all).
- * No counterpart in the reference (its launcher allocates its own temporary). */
+/* Same computation with a caller-provided workspace: 16-byte aligned, at least
+ * mpk_gemm_workspace_size() bytes (plus K*N*2 when B is not 16-byte aligned), and
+ * not used by other work in flight until this call's kernels have finished on
+ * `stream`.  With workspace == NULL the on-chip conversion kernel runs (no
+ * workspace at all; its shape and alignment limits apply).  No counterpart in the
+ * reference (its launcher allocates its own temporary). */
 int mpk_gemm_mxfp8_bf16_ws(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
                            const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                            uint8_t* D_scales, int M, int N, int K, void* workspace,
                            size_t workspace_bytes, void* stream);
 
-/* Workspace bytes mpk_gemm_mxfp8_bf16_ws needs for an M x N x K product. */
+/* Workspace bytes mpk_gemm_mxfp8_bf16_ws needs for an M x N x K product with a
+ * 16-byte aligned B: M * roundup(K, 8) * 2, rounded up to 256, plus
+ * K * roundup(N, 8) * 2 when N % 8 != 0. */
 int mpk_gemm_workspace_size(int M, int N, int K, size_t* bytes);
 
 /* Returns the current device's pooled GEMM workspace to the driver, once the
@@ -77,15 +82,17 @@ int mpk_gemm_workspace_size(int M, int N, int K, size_t* bytes);
 int mpk_release_workspace_pool(void);
 
 /* Fixed size of the device array behind mpk_gemm_mxfp8_bf16_noalloc: 32 MiB per
- * device, enough for the BF16 copy of an A with M*K <= 16,777,216 (4096 x 4096). */
+ * device, enough for the BF16 copy of an A with M*K <= 16,777,216 (4096 x 4096) when
+ * K % 8 == 0, N % 8 == 0 and B is 16-byte aligned (other shapes need the workspace
+ * that mpk_gemm_mxfp8_bf16_ws describes). */
 #define MPK_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 
 /* Same computation as mpk_gemm_mxfp8_bf16, for callers that may not allocate
  * device memory once running (a caching allocator that has reserved the device, a
  * latency-bound loop, a fixed memory budget).  The A workspace is a fixed array in
  * the library's device image (MPK_NOALLOC_SCRATCH_BYTES per device, held from
- * the image's load); this call allocates nothing.  Sizes with M*K*2 above that
- * return MPK_ERR_UNSUPPORTED.  Nothing in the array needs to start at zero.
+ * the image's load); this call allocates nothing.  Sizes whose workspace exceeds
+ * that return MPK_ERR_UNSUPPORTED.  Nothing in the array needs to start at zero.
  * All calls on a device share the array: calls that can run at the same time
  * (different streams without an event between them, or unordered host threads)
  * race, so issue them on one stream or order them.  The first call on each device

@@ -131,8 +131,8 @@ const char* mpk_status_string(int status)
     switch (status) {
     case MPK_SUCCESS: return "success";
     case MPK_ERR_INVALID_VALUE: return "invalid value (null pointer or negative size)";
-    case MPK_ERR_UNSUPPORTED: return "unsupported shape (GEMM needs K % 16 == 0 and N % 8 == 0)";
-    case MPK_ERR_MISALIGNED: return "misaligned pointer (A_data and B must be 16-byte aligned)";
+    case MPK_ERR_UNSUPPORTED: return "shape or size not supported by this entry point";
+    case MPK_ERR_MISALIGNED: return "pointer alignment not supported by this entry point";
     case MPK_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait expired";
     case MPK_ERR_ARCH: return "current device is not sm_100";
     case MPK_ERR_DRIVER: return "CUDA driver entry point or tensor-map encoding failed";
@@ -170,16 +170,7 @@ static int validate_gemm(const uint8_t* A_data, const uint8_t* A_scales, const v
     // The reference adds C only when both C pointers are set
     // (src/kernels/gemm_fp8_tensorcore.cu:188).
     if (!C_data || !C_scales) C_data = nullptr, C_scales = nullptr;
-    if (int rc = check_arch()) return rc;
-    if (K > 0 && (K % 16 != 0 || N % 8 != 0)) {
-        set_last_error("GEMM needs K %% 16 == 0 and N %% 8 == 0 (TMA row strides); got N=%d K=%d", N, K);
-        return MPK_ERR_UNSUPPORTED;
-    }
-    if (K > 0 && ((reinterpret_cast<uintptr_t>(A_data) & 15u) || (reinterpret_cast<uintptr_t>(B_bf16) & 15u))) {
-        set_last_error("A_data and B must be 16-byte aligned for TMA");
-        return MPK_ERR_MISALIGNED;
-    }
-    return MPK_SUCCESS;
+    return check_arch();
 }
 
 // Stream-ordered pool of one device for the A workspace of mpk_gemm_mxfp8_bf16.
@@ -242,7 +233,8 @@ int mpk_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const vo
     if (cs == cudaStreamCaptureStatusNone) {
         if (cudaMemPool_t pool = workspace_pool(true)) {
             void* ws = nullptr;
-            if (cudaMallocFromPoolAsync(&ws, gemm_workspace_bytes(M, K), pool, st) == cudaSuccess) {
+            const size_t need = gemm_workspace_bytes(M, N, K, gemm_b_needs_copy(B_bf16, N));
+            if (cudaMallocFromPoolAsync(&ws, need, pool, st) == cudaSuccess) {
                 const int rc = launch_gemm_mxfp8_bf16_prepass(A_data, A_scales, B_bf16, C_data, C_scales,
                                                               D_data, D_scales, M, N, K, ws, st);
                 const cudaError_t fe = cudaFreeAsync(ws, st);
@@ -251,6 +243,7 @@ int mpk_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const vo
             cudaGetLastError();
         }
     }
+    if (int rc = check_onchip_gemm_shape(A_data, B_bf16, N, K)) return rc;
     return launch_gemm_mxfp8_bf16(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales, M, N,
                                   K, st);
 }
@@ -265,7 +258,7 @@ int mpk_release_workspace_pool(void)
 int mpk_gemm_workspace_size(int M, int N, int K, size_t* bytes)
 {
     if (!bytes || M < 0 || N < 0 || K < 0) return MPK_ERR_INVALID_VALUE;
-    *bytes = gemm_workspace_bytes(M, K);
+    *bytes = gemm_workspace_bytes(M, N, K, N % 8 != 0);
     return MPK_SUCCESS;
 }
 
@@ -282,12 +275,18 @@ int mpk_gemm_mxfp8_bf16_ws(const uint8_t* A_data, const uint8_t* A_scales, const
         return from_cuda(launch_mxfp8_requantize(C_data, C_scales, D_data, D_scales, M, N,
                                                  (cudaStream_t)stream),
                          "requantize launch");
-    if (!workspace)
+    if (!workspace) {
+        if (int rc = check_onchip_gemm_shape(A_data, B_bf16, N, K)) return rc;
         return launch_gemm_mxfp8_bf16(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales, M,
                                       N, K, (cudaStream_t)stream);
-    const size_t need = gemm_workspace_bytes(M, K);
+    }
+    const bool copy_b = gemm_b_needs_copy(B_bf16, N);
+    const size_t need = gemm_workspace_bytes(M, N, K, copy_b);
     if (workspace_bytes < need) {
-        set_last_error("workspace of %zu bytes needed (M*K*2), got %zu", need, workspace_bytes);
+        set_last_error("workspace of %zu bytes needed%s, got %zu", need,
+                       copy_b && N % 8 == 0 ? " (B is not 16-byte aligned, so a padded copy of B is "
+                                              "included)" : "",
+                       workspace_bytes);
         return MPK_ERR_INVALID_VALUE;
     }
     if (reinterpret_cast<uintptr_t>(workspace) & 15u) {
@@ -348,7 +347,7 @@ int mpk_mxfp8_dequantize_bf16(const uint8_t* data, const uint8_t* scales, void* 
         return MPK_ERR_MISALIGNED;
     }
     if (int rc = check_arch()) return rc;
-    return from_cuda(launch_mxfp8_dequantize_bf16(data, scales, output, M, K, (cudaStream_t)stream),
+    return from_cuda(launch_mxfp8_dequantize_bf16(data, scales, output, M, K, K, (cudaStream_t)stream),
                      "dequantize-bf16 launch");
 }
 
@@ -475,10 +474,11 @@ extern "C" int mpk_gemm_mxfp8_bf16_noalloc(const uint8_t* A_data, const uint8_t*
     if (K == 0)
         return from_cuda(launch_mxfp8_requantize(C_data, C_scales, D_data, D_scales, M, N, st),
                          "requantize launch");
-    const size_t need = gemm_workspace_bytes(M, K);
+    const size_t need = gemm_workspace_bytes(M, N, K, gemm_b_needs_copy(B_bf16, N));
     if (need > (size_t)MPK_NOALLOC_SCRATCH_BYTES) {
-        set_last_error("mpk_gemm_mxfp8_bf16_noalloc: M*K*2 = %zu bytes exceeds its fixed scratch of %zu "
-                       "bytes (M*K <= %zu); use mpk_gemm_mxfp8_bf16 or mpk_gemm_mxfp8_bf16_ws",
+        set_last_error("mpk_gemm_mxfp8_bf16_noalloc: the workspace of %zu bytes exceeds its fixed scratch "
+                       "of %zu bytes (M*K <= %zu for K %% 8 == 0, N %% 8 == 0 and 16-byte aligned B); use "
+                       "mpk_gemm_mxfp8_bf16 or mpk_gemm_mxfp8_bf16_ws",
                        need, (size_t)MPK_NOALLOC_SCRATCH_BYTES, (size_t)MPK_NOALLOC_SCRATCH_BYTES / 2);
         return MPK_ERR_UNSUPPORTED;
     }

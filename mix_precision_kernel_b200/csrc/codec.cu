@@ -257,16 +257,17 @@ mxfp8_dequantize_bf16_flat_kernel(const uint8_t* __restrict__ data, const uint8_
     }
 }
 
-// Any shape: one element per thread.
+// Any shape and alignment, output rows ld_out elements apart: one element per thread.
 __global__ void __launch_bounds__(kCodecThreads)
 mxfp8_dequantize_bf16_elem_kernel(const uint8_t* __restrict__ data, const uint8_t* __restrict__ scales,
-                                  uint16_t* __restrict__ out, int64_t M, int64_t K, int64_t nblk)
+                                  uint16_t* __restrict__ out, int64_t M, int64_t K, int64_t nblk,
+                                  int64_t ld_out)
 {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M * K; i += stride) {
         const int64_t row = i / K, k = i % K;
         const float v = e4m3x2_to_f32x2(data[i]).x * e8m0_to_f32(scales[row * nblk + k / 32]);
-        out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+        out[row * ld_out + k] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
     }
 }
 
@@ -317,18 +318,18 @@ cudaError_t launch_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, 
 }
 
 cudaError_t launch_mxfp8_dequantize_bf16(const uint8_t* data, const uint8_t* scales, void* out,
-                                         int64_t M, int64_t K, cudaStream_t stream)
+                                         int64_t M, int64_t K, int64_t ld_out, cudaStream_t stream)
 {
     const int64_t nblk = (K + 31) / 32;
     if (M == 0 || K == 0) return cudaSuccess;
     uint16_t* o = static_cast<uint16_t*>(out);
-    if (K % 32 == 0 && aligned16(out) && (reinterpret_cast<uintptr_t>(data) & 7u) == 0) {
+    if (K % 32 == 0 && ld_out == K && aligned16(out) && (reinterpret_cast<uintptr_t>(data) & 7u) == 0) {
         const int64_t no = M * K / 8;
         mxfp8_dequantize_bf16_flat_kernel<<<codec_grid(no / kPrepassU), kCodecThreads, 0, stream>>>(
             data, scales, o, no);
     } else {
         mxfp8_dequantize_bf16_elem_kernel<<<codec_grid(M * K), kCodecThreads, 0, stream>>>(
-            data, scales, o, M, K, nblk);
+            data, scales, o, M, K, nblk, ld_out);
     }
     return cudaGetLastError();
 }

@@ -981,9 +981,11 @@ namespace {
 
 // Shared host setup of both GEMM kernels: device checks, status word, B tensor map
 // and the kernel parameters.
-int gemm_setup(const uint8_t* A_scales, const void* B, const uint8_t* C_data, const uint8_t* C_scales,
-               uint8_t* D_data, uint8_t* D_scales, int M, int N, int K, int& dev,
-               PFN_cuTensorMapEncodeTiled_v12000& enc, CUtensorMap& tmap_b, gemm::Params& p)
+// B's tensor map covers N x K elements with rows ldb elements apart (ldb >= N, a
+// multiple of 8); columns past N read as zeros.
+int gemm_setup(const uint8_t* A_scales, const void* B, int ldb, const uint8_t* C_data,
+               const uint8_t* C_scales, uint8_t* D_data, uint8_t* D_scales, int M, int N, int K,
+               int& dev, PFN_cuTensorMapEncodeTiled_v12000& enc, CUtensorMap& tmap_b, gemm::Params& p)
 {
     using namespace gemm;
     int rc = get_device(dev);
@@ -992,7 +994,7 @@ int gemm_setup(const uint8_t* A_scales, const void* B, const uint8_t* C_data, co
     if ((rc = status_ptr(dev, &status))) return rc;
     if ((rc = get_encoder(&enc))) return rc;
     if ((rc = encode_2d(enc, &tmap_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, B, (uint64_t)N, (uint64_t)K,
-                        (uint64_t)N * 2, 64, BK, CU_TENSOR_MAP_SWIZZLE_128B)))
+                        (uint64_t)ldb * 2, 64, BK, CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
     p.A_scales = A_scales;
     p.C_data = C_data;
@@ -1060,7 +1062,39 @@ bool g_smem_attr_bf16a[64] = {};
 
 }  // namespace
 
-size_t gemm_workspace_bytes(int M, int K) { return (size_t)M * (size_t)K * 2u; }
+namespace {
+constexpr size_t kWsAlign = 256;
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+int64_t padded8(int x) { return ((int64_t)x + 7) / 8 * 8; }
+}  // namespace
+
+int check_onchip_gemm_shape(const uint8_t* A_data, const void* B, int N, int K)
+{
+    if (K % 16 != 0 || N % 8 != 0) {
+        set_last_error("the on-chip conversion kernel needs K %% 16 == 0 and N %% 8 == 0 (TMA row strides); "
+                       "got N=%d K=%d -- pass a workspace (mpk_gemm_mxfp8_bf16_ws) for other shapes",
+                       N, K);
+        return MPK_ERR_UNSUPPORTED;
+    }
+    if ((reinterpret_cast<uintptr_t>(A_data) & 15u) || (reinterpret_cast<uintptr_t>(B) & 15u)) {
+        set_last_error("the on-chip conversion kernel needs A_data and B 16-byte aligned (TMA) -- "
+                       "pass a workspace (mpk_gemm_mxfp8_bf16_ws) for other pointers");
+        return MPK_ERR_MISALIGNED;
+    }
+    return MPK_SUCCESS;
+}
+
+bool gemm_b_needs_copy(const void* B, int N)
+{
+    return N % 8 != 0 || (reinterpret_cast<uintptr_t>(B) & 15u) != 0;
+}
+
+size_t gemm_workspace_bytes(int M, int N, int K, bool copy_b)
+{
+    size_t bytes = round_up((size_t)M * (size_t)padded8(K) * 2u, kWsAlign);
+    if (copy_b) bytes += (size_t)K * (size_t)padded8(N) * 2u;
+    return bytes;
+}
 
 int launch_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const void* B,
                            const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
@@ -1071,7 +1105,7 @@ int launch_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const
     PFN_cuTensorMapEncodeTiled_v12000 enc;
     CUtensorMap tmap_a, tmap_b;
     Params p;
-    int rc = gemm_setup(A_scales, B, C_data, C_scales, D_data, D_scales, M, N, K, dev, enc, tmap_b, p);
+    int rc = gemm_setup(A_scales, B, N, C_data, C_scales, D_data, D_scales, M, N, K, dev, enc, tmap_b, p);
     if (rc) return rc;
     if ((rc = encode_2d(enc, &tmap_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, A_data, (uint64_t)K, (uint64_t)M,
                         (uint64_t)K, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
@@ -1109,14 +1143,29 @@ int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scale
     PFN_cuTensorMapEncodeTiled_v12000 enc;
     CUtensorMap tmap_a16, tmap_b;
     Params p;
-    int rc = gemm_setup(A_scales, B, C_data, C_scales, D_data, D_scales, M, N, K, dev, enc, tmap_b, p);
+    // Workspace: A's BF16 copy [M][lda], then (when needed) B's padded copy [K][ldb].
+    const int64_t lda = padded8(K);
+    const bool copy_b = gemm_b_needs_copy(B, N);
+    const int64_t ldb = copy_b ? padded8(N) : N;
+    void* b_copy = static_cast<uint8_t*>(workspace) + round_up((size_t)M * (size_t)lda * 2u, kWsAlign);
+    const void* b_used = copy_b ? b_copy : B;
+    int rc = gemm_setup(A_scales, b_used, (int)ldb, C_data, C_scales, D_data, D_scales, M, N, K, dev, enc,
+                        tmap_b, p);
     if (rc) return rc;
     if ((rc = encode_2d(enc, &tmap_a16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, workspace, (uint64_t)K,
-                        (uint64_t)M, (uint64_t)K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+                        (uint64_t)M, (uint64_t)lda * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
     if ((rc = ensure_smem_attr((const void*)gemm_bf16a_mxfp8_kernel, P_SMEM_BYTES, &g_smem_attr_bf16a[dev])))
         return rc;
-    cudaError_t e = launch_mxfp8_dequantize_bf16(A_data, A_scales, workspace, M, K, stream);
+    if (copy_b) {
+        const cudaError_t ce = cudaMemcpy2DAsync(b_copy, (size_t)ldb * 2, B, (size_t)N * 2, (size_t)N * 2,
+                                                 (size_t)K, cudaMemcpyDeviceToDevice, stream);
+        if (ce != cudaSuccess) {
+            set_last_error("B row-padding copy failed: %s", cudaGetErrorString(ce));
+            return (int)ce;
+        }
+    }
+    cudaError_t e = launch_mxfp8_dequantize_bf16(A_data, A_scales, workspace, M, K, lda, stream);
     if (e != cudaSuccess) {
         set_last_error("A pre-pass launch failed: %s", cudaGetErrorString(e));
         return (int)e;

@@ -18,7 +18,7 @@ cudaError_t launch_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, 
                                     int64_t M, int64_t K, cudaStream_t stream);
 // MXFP8 [M][K] -> BF16 [M][K] (exact for scale bytes other than 1 and 2).
 cudaError_t launch_mxfp8_dequantize_bf16(const uint8_t* data, const uint8_t* scales, void* out,
-                                         int64_t M, int64_t K, cudaStream_t stream);
+                                         int64_t M, int64_t K, int64_t ld_out, cudaStream_t stream);
 // D = MXFP8(dequant(C)) along N (C may be null: D = MXFP8(0)).  The K == 0 GEMM.
 cudaError_t launch_mxfp8_requantize(const uint8_t* c_data, const uint8_t* c_scales, uint8_t* d_data,
                                     uint8_t* d_scales, int64_t M, int64_t N, cudaStream_t stream);
@@ -28,9 +28,18 @@ int launch_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const
                            const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                            uint8_t* D_scales, int M, int N, int K, cudaStream_t stream);
 
-// GEMM with the A operand dequantized to BF16 into `workspace` (gemm_workspace_bytes)
-// by a pre-pass, then streamed by TMA.
-size_t gemm_workspace_bytes(int M, int K);
+// The on-chip conversion kernel's requirements: K % 16 == 0, N % 8 == 0, A_data and B
+// 16-byte aligned (TMA row strides and base addresses).  Returns 0 or an MPK status
+// with the detail set.
+int check_onchip_gemm_shape(const uint8_t* A_data, const void* B, int N, int K);
+
+// GEMM with the A operand dequantized to BF16 by a pre-pass into `workspace`, then
+// streamed by TMA.  Any M, N, K and alignment: A's BF16 copy has rows padded to a
+// multiple of 8 elements, and B is copied into the workspace with padded rows when
+// N % 8 != 0 or B is not 16-byte aligned (gemm_b_needs_copy).  `workspace` must be
+// 16-byte aligned and hold gemm_workspace_bytes(M, N, K, gemm_b_needs_copy(B, N)).
+bool gemm_b_needs_copy(const void* B, int N);
+size_t gemm_workspace_bytes(int M, int N, int K, bool copy_b);
 int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scales, const void* B,
                                    const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                                    uint8_t* D_scales, int M, int N, int K, void* workspace,

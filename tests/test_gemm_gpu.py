@@ -175,6 +175,8 @@ def test_invalid_arguments(mpk_lib, cuda):
 
     buf = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
     b16 = torch.zeros(1 << 19, dtype=torch.bfloat16, device="cuda")
+    # The on-chip conversion kernel (no workspace) has TMA's shape and alignment
+    # limits; the default entry point takes every shape (test_any_shape_and_alignment).
     cases = [
         (dict(M=64, N=64, K=40), MPK_ERR_UNSUPPORTED),
         (dict(M=64, N=60, K=64), MPK_ERR_UNSUPPORTED),
@@ -184,13 +186,57 @@ def test_invalid_arguments(mpk_lib, cuda):
     for args, want in cases:
         a = buf.data_ptr() + args.get("a_off", 0)
         with pytest.raises(MpkError) as e:
-            mpk_lib.gemm_fp8_tensorcore(a, buf.data_ptr(), b16.data_ptr(), None, None, buf.data_ptr(),
-                                        buf.data_ptr(), args["M"], args["N"], args["K"])
+            mpk_lib.gemm_fp8_tensorcore_ws(a, buf.data_ptr(), b16.data_ptr(), None, None, buf.data_ptr(),
+                                           buf.data_ptr(), args["M"], args["N"], args["K"], None)
         assert e.value.status == want
+    with pytest.raises(MpkError) as e:
+        mpk_lib.gemm_fp8_tensorcore(buf.data_ptr(), buf.data_ptr(), b16.data_ptr(), None, None,
+                                    buf.data_ptr(), buf.data_ptr(), -1, 64, 64)
+    assert e.value.status == MPK_ERR_INVALID_VALUE
     with pytest.raises(MpkError) as e:
         mpk_lib.gemm_fp8_tensorcore(None, None, None, None, None, None, None, 8, 8, 16)
     assert e.value.status == MPK_ERR_INVALID_VALUE
     assert mpk_lib.device_status() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(100, 100, 100), (37, 1000, 33), (130, 36, 4100), (1, 1, 1),
+                                   (65, 7, 17), (300, 520, 1112), (64, 2050, 96), (257, 300, 40)])
+@pytest.mark.parametrize("with_c", [True, False])
+def test_any_shape(mpk_lib, cuda, M, N, K, with_c):
+    """Shapes outside TMA's stride rules (K % 16 != 0, N % 8 != 0): the pre-pass pads
+    A's BF16 rows, B is copied with padded rows, and D matches the gold."""
+    inp = O.make_gemm_inputs(M, N, K, seed=M * 7 + N + K, with_c=with_c)
+    Dd, Ds = run_gemm(mpk_lib, inp, with_c=with_c)
+    check_parity(Dd, Ds, O.gold_mx(inp), f"any shape {M}x{N}x{K} C={with_c}")
+
+
+@pytest.mark.parametrize("a_off,b_off,c_off,d_off", [(1, 0, 0, 0), (0, 2, 0, 0), (3, 6, 5, 7), (8, 8, 1, 1)])
+def test_any_alignment(mpk_lib, cuda, a_off, b_off, c_off, d_off):
+    """A, B, C and D at byte offsets that break 16-byte alignment (B by whole BF16
+    elements): the same D as with aligned buffers."""
+    import torch
+
+    M, N, K = 192, 320, 256
+    inp = O.make_gemm_inputs(M, N, K, seed=11)
+    want_d, want_s = run_gemm(mpk_lib, inp)
+
+    def at(a, off):
+        t = to_dev(a)
+        raw = t.view(torch.uint8).reshape(-1)
+        big = torch.empty(raw.numel() + off, dtype=torch.uint8, device="cuda")
+        big[off:].copy_(raw)
+        return big, big.data_ptr() + off
+
+    Ab, A = at(inp["A_data"], a_off)
+    Bb, B = at(inp["B_bf16"], b_off)
+    Cb, C = at(inp["C_data"], c_off)
+    As, Cs = to_dev(inp["A_scales"]), to_dev(inp["C_scales"])
+    Db = torch.full((M * N + d_off,), 0xEE, dtype=torch.uint8, device="cuda")
+    Ds = torch.full((M, N // 32), 0xEE, dtype=torch.uint8, device="cuda")
+    mpk_lib.gemm_fp8_tensorcore(A, As, B, C, Cs, Db.data_ptr() + d_off, Ds, M, N, K)
+    torch.cuda.synchronize()
+    got_d = to_host(Db)[d_off:].reshape(M, N)
+    assert np.array_equal(got_d, want_d) and np.array_equal(to_host(Ds), want_s)
 
 
 def test_stream_graph_capture_and_determinism(mpk_lib, cuda):

@@ -45,6 +45,20 @@ def test_ws_ragged(mpk_lib, cuda, M, N, K, with_c):
     check_parity(Dd, Ds, O.gold_mx(inp), f"ws ragged {M}x{N}x{K} C={with_c}")
 
 
+@pytest.mark.parametrize("M,N,K", [(100, 100, 100), (65, 7, 17), (64, 2050, 96)])
+def test_ws_any_shape(mpk_lib, cuda, M, N, K):
+    """Shapes outside TMA's stride rules need the padded workspace, whose size
+    mpk_gemm_workspace_size reports; the on-chip kernel refuses them."""
+    inp = O.make_gemm_inputs(M, N, K, seed=M + 2 * N + K)
+    d0, s0 = run_gemm(mpk_lib, inp)
+    d1, s1 = run_gemm(mpk_lib, inp, path="workspace")
+    assert np.array_equal(d0, d1) and np.array_equal(s0, s1)
+    check_parity(d1, s1, O.gold_mx(inp), f"ws any shape {M}x{N}x{K}")
+    with pytest.raises(mpk_lib.MpkError) as e:
+        run_gemm(mpk_lib, inp, path="onchip")
+    assert e.value.status == mpk_lib.MPK_ERR_UNSUPPORTED
+
+
 @pytest.mark.parametrize("with_nan", [False, True])
 def test_ws_exotic_scales_and_nan_codes(mpk_lib, cuda, with_nan):
     """Scale bytes 0-2, 134/135 and 247-255 and NaN codes take the pre-pass's
@@ -102,6 +116,7 @@ def test_ws_argument_checks(mpk_lib, cuda):
     Ds = torch.empty((M, N // 32), dtype=torch.uint8, device="cuda")
     need = mpk_lib.gemm_workspace_size(M, N, K)
     assert need == M * K * 2
+    assert mpk_lib.gemm_workspace_size(100, 100, 100) == 100 * 104 * 2 + (256 - 100 * 104 * 2 % 256) + 100 * 104 * 2
     small = torch.empty((need - 16,), dtype=torch.uint8, device="cuda")
     with pytest.raises(mpk_lib.MpkError) as e:
         mpk_lib.gemm_fp8_tensorcore_ws(A, As, B, None, None, D, Ds, M, N, K, small)
