@@ -325,40 +325,85 @@ def run_gemm_arm(args, world, rank, local, dist):
     e1.record(stream)
     barrier_sync(dist)
     pre_ms = e0.elapsed_time(e1) / args.steps
-    del ws
+    # Library bar: cuBLAS BF16 x BF16 -> BF16 (torch.matmul) on the same, already
+    # dequantized A and B -- a plain GEMM without the C term or the MXFP8 epilogue.
+    lib_steps = min(args.steps, 100)
+    out16 = torch.matmul(ws, B)
+    for _ in range(3):
+        torch.matmul(ws, B, out=out16)
+    barrier_sync(dist)
+    e0.record(stream)
+    for _ in range(lib_steps):
+        torch.matmul(ws, B, out=out16)
+    e1.record(stream)
+    barrier_sync(dist)
+    lib_ms = e0.elapsed_time(e1) / lib_steps
+    del ws, out16
     gemm_ms = ms / args.steps - pre_ms
     kernel_tflops = flops / (gemm_ms / 1e3) / 1e12
     step_tflops = flops / (ms / args.steps / 1e3) / 1e12
 
-    # end to end through the C ABI with host buffers
+    # End to end through the C ABI with host buffers.  Every step uploads all of its
+    # inputs (A, A scales, B, C, C scales) from pinned host memory and downloads its
+    # D and D scales.  Two device buffer sets and three streams (upload, GEMM,
+    # download) let step i+1's upload and step i-1's download run beside step i's
+    # kernels, as a serving loop would pipeline them.
     hA = torch.empty_like(Ad, device="cpu").pin_memory(); hA.copy_(Ad)
     hAs = torch.empty_like(As, device="cpu").pin_memory(); hAs.copy_(As)
     hB = torch.empty_like(B, device="cpu").pin_memory(); hB.copy_(B)
     hC = torch.empty_like(Cd, device="cpu").pin_memory(); hC.copy_(Cd)
     hCs = torch.empty_like(Cs, device="cpu").pin_memory(); hCs.copy_(Cs)
-    hD = torch.empty_like(D, device="cpu").pin_memory()
-    hDs = torch.empty_like(Ds, device="cpu").pin_memory()
+    hD = [torch.empty_like(D, device="cpu").pin_memory() for _ in range(2)]
+    hDs = [torch.empty_like(Ds, device="cpu").pin_memory() for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in (hA, hAs, hB, hC, hCs))
-    d2h = hD.numel() + hDs.numel()
+    d2h = hD[0].numel() + hDs[0].numel()
+    bufs = [(Ad, As, B, Cd, Cs, D, Ds),
+            tuple(torch.empty_like(t) for t in (Ad, As, B, Cd, Cs, D, Ds))]
+    s_up, s_down = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]    # set k's inputs uploaded
+    ev_used = [torch.cuda.Event() for _ in range(2)]  # set k's GEMM done (inputs free, D ready)
+    ev_out = [torch.cuda.Event() for _ in range(2)]   # set k's D downloaded (D free)
+    for k in range(2):
+        ev_used[k].record(stream)
+        ev_out[k].record(stream)
 
-    def e2e_step():
-        Ad.copy_(hA, non_blocking=True); As.copy_(hAs, non_blocking=True)
-        B.copy_(hB, non_blocking=True); Cd.copy_(hC, non_blocking=True)
-        Cs.copy_(hCs, non_blocking=True)
-        step()
-        hD.copy_(D, non_blocking=True); hDs.copy_(Ds, non_blocking=True)
+    def e2e_step(i):
+        k = i % 2
+        a_d, a_s, b_, c_d, c_s, d_d, d_s = bufs[k]
+        s_up.wait_event(ev_used[k])
+        with torch.cuda.stream(s_up):
+            for dst, src in ((a_d, hA), (a_s, hAs), (b_, hB), (c_d, hC), (c_s, hCs)):
+                dst.copy_(src, non_blocking=True)
+        ev_in[k].record(s_up)
+        stream.wait_event(ev_in[k])
+        stream.wait_event(ev_out[k])
+        rc = L.mpk_gemm_mxfp8_bf16(a_d.data_ptr(), a_s.data_ptr(), b_.data_ptr(), c_d.data_ptr(),
+                                   c_s.data_ptr(), d_d.data_ptr(), d_s.data_ptr(), M, N, K, sptr)
+        if rc:
+            raise mpk.MpkError(rc, L.mpk_last_error().decode())
+        ev_used[k].record(stream)
+        s_down.wait_event(ev_used[k])
+        with torch.cuda.stream(s_down):
+            hD[k].copy_(d_d, non_blocking=True)
+            hDs[k].copy_(d_s, non_blocking=True)
+        ev_out[k].record(s_down)
 
     e2e_steps = max(3, min(args.steps, 20))
-    for _ in range(2):
-        e2e_step()
+    for i in range(2):
+        e2e_step(i)
     barrier_sync(dist)
     e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
+    s_up.wait_event(e0)
+    for i in range(2, 2 + e2e_steps):
+        e2e_step(i)
+    for k in range(2):
+        stream.wait_event(ev_out[k])
     e1.record(stream)
     barrier_sync(dist)
     e2e_ms = max_over_ranks(dist, e0.elapsed_time(e1))
     e2e_value = world * flops * e2e_steps / (e2e_ms / 1e3) / 1e12
+    same = bool(torch.equal(hD[0], hD[1])) and bool(torch.equal(hDs[0].to(D.device), Ds))
+    del bufs
 
     # Denominator: the burst cuBLAS figure, unless the clock record shows the power
     # cap acting during the timed region, in which case the sustained figure (the
@@ -400,8 +445,15 @@ def run_gemm_arm(args, world, rank, local, dist):
         "gpu_launches": 2 * args.steps,
         "pct_of_bf16_peak": round(100.0 * value / world / burst, 2),
         "e2e": {"value": round(e2e_value, 3), "unit": "TFLOPS", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps, "ms_per_step": round(e2e_ms / e2e_steps, 4),
+                "pipelining": "two buffer sets; upload, GEMM and download streams overlap across steps",
+                "downloads_match_device_result": same},
         "roofline": roofline,
+        "library_bar": {"what": "cuBLAS BF16xBF16->BF16 GEMM (torch.matmul) on the pre-dequantized A; "
+                                "no C term, no MXFP8 epilogue",
+                        "tflops": round(flops / (lib_ms / 1e3) / 1e12, 2), "ms": round(lib_ms, 5),
+                        "gemm_kernel_over_library": round(lib_ms / gemm_ms, 4),
+                        "step_over_library": round(lib_ms / (ms / args.steps), 4)},
         "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
     }
     line["clocks"]["samples"] = clocks["samples"]
@@ -440,6 +492,12 @@ def run_codec_arm(args, world, rank, local, dist):
 
     q_ms = timed(lambda: L.mpk_mxfp8_quantize(x.data_ptr(), d.data_ptr(), s.data_ptr(), M, K, sptr))
     dq_ms = timed(lambda: L.mpk_mxfp8_dequantize(d.data_ptr(), s.data_ptr(), y.data_ptr(), M, K, sptr))
+    # Companion kernels, reported beside the headline pair: BF16 -> MXFP8 and MXFP8 -> BF16.
+    x16 = x.to(torch.bfloat16)
+    del y
+    qb_ms = timed(lambda: L.mpk_mxfp8_quantize_bf16(x16.data_ptr(), d.data_ptr(), s.data_ptr(), M, K, sptr))
+    db_ms = timed(lambda: L.mpk_mxfp8_dequantize_bf16(d.data_ptr(), s.data_ptr(), x16.data_ptr(), M, K, sptr))
+    bytes16 = M * K * 2 + M * K + M * K // 32
     peaks, src = load_peaks()
     hbm = float(peaks["hbm_gbs"])
     qg, dg = bytes_one / q_ms / 1e6, bytes_one / dq_ms / 1e6
@@ -453,6 +511,11 @@ def run_codec_arm(args, world, rank, local, dist):
         "config": {"workload": "codec quantize+dequantize", "M": M, "K": K,
                    "l2": "1 GiB FP32 tensor > L2"},
         "gpu_launches": 2 * args.steps,
+        "bf16_companions": {"quantize_bf16_gbs": round(bytes16 / qb_ms / 1e6, 1),
+                            "quantize_bf16_frac": round(bytes16 / qb_ms / 1e6 / hbm, 4),
+                            "dequantize_bf16_gbs": round(bytes16 / db_ms / 1e6, 1),
+                            "dequantize_bf16_frac": round(bytes16 / db_ms / 1e6 / hbm, 4),
+                            "bytes_per_launch": bytes16},
         "roofline": {"bound": "hbm", "achieved": round(qg, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(qg / hbm, 4), "traffic": load_traffic("mxfp8_quantize_flat_kernel", "codec"),
                      "peak_source": f"{src} hbm_gbs", "dequantize_gbs": round(dg, 1),

@@ -114,6 +114,13 @@ int mpk_mxfp8_quantize(const float* input, uint8_t* data, uint8_t* scales, int M
 int mpk_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, float* output, int M, int K,
                          void* stream);
 
+/* BF16 [M][K] (bit patterns, 2-byte aligned) -> MXFP8 along K: the quantizer of
+ * mpk_mxfp8_quantize applied to each value widened exactly to FP32, for producers of
+ * A that hold BF16 activations.  No counterpart in the reference (its quantizer
+ * takes FP32 only). */
+int mpk_mxfp8_quantize_bf16(const void* input, uint8_t* data, uint8_t* scales, int M, int K,
+                            void* stream);
+
 /* MXFP8 [M][K] -> BF16 [M][K] (bit patterns, 2-byte aligned output): code x
  * 2^(scale-127) rounded to nearest even, which is exact for scale bytes >= 3.
  * This is the A pre-pass of mpk_gemm_mxfp8_bf16.  No counterpart in the reference

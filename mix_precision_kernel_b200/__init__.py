@@ -27,7 +27,7 @@ __all__ = [
     "gemm_fp8_tensorcore", "mxfp8_quantize_gpu", "mxfp8_dequantize_gpu",
     "mxfp8_quantize_host", "mxfp8_dequantize_host",
     "gemm_fp8_tensorcore_ws", "gemm_workspace_size", "release_workspace_pool",
-    "mxfp8_dequantize_bf16_gpu", "gemm_fp8_tensorcore_noalloc", "NOALLOC_SCRATCH_BYTES",
+    "mxfp8_dequantize_bf16_gpu", "mxfp8_quantize_bf16_gpu", "gemm_fp8_tensorcore_noalloc", "NOALLOC_SCRATCH_BYTES",
     "gemm", "quantize", "dequantize", "device_status", "set_wait_timeout_ns", "wait_selftest",
     "MX_BLOCK", "nblk",
 ]
@@ -80,6 +80,7 @@ def lib() -> ctypes.CDLL:
             L.mpk_mxfp8_quantize.argtypes = [vp, vp, vp, ci, ci, vp]
             L.mpk_mxfp8_dequantize.argtypes = [vp, vp, vp, ci, ci, vp]
             L.mpk_mxfp8_dequantize_bf16.argtypes = [vp, vp, vp, ci, ci, vp]
+            L.mpk_mxfp8_quantize_bf16.argtypes = [vp, vp, vp, ci, ci, vp]
             L.mpk_mxfp8_quantize_host.argtypes = [vp, u8p, u8p, ci, ci]
             L.mpk_mxfp8_dequantize_host.argtypes = [u8p, u8p, vp, ci, ci]
             L.mpk_device_status.argtypes = [ctypes.POINTER(ci)]
@@ -92,6 +93,7 @@ def lib() -> ctypes.CDLL:
             for f in ("mpk_gemm_mxfp8_bf16", "mpk_gemm_mxfp8_bf16_ws", "mpk_gemm_workspace_size",
                       "mpk_release_workspace_pool", "mpk_mxfp8_quantize", "mpk_mxfp8_dequantize",
                       "mpk_mxfp8_dequantize_bf16", "mpk_gemm_mxfp8_bf16_noalloc",
+                      "mpk_mxfp8_quantize_bf16",
                       "mpk_mxfp8_quantize_host", "mpk_mxfp8_dequantize_host", "mpk_device_status",
                       "mpk_set_wait_timeout_ns", "mpk_wait_selftest", "mpk_version"):
                 getattr(L, f).restype = ci
@@ -196,6 +198,12 @@ def mxfp8_quantize_gpu(input, data, scales, M: int, K: int, stream=None) -> None
 def mxfp8_dequantize_gpu(data, scales, output, M: int, K: int, stream=None) -> None:
     s = _stream(stream, data, output)
     _check(lib().mpk_mxfp8_dequantize(_addr(data), _addr(scales), _addr(output), M, K, s))
+
+
+def mxfp8_quantize_bf16_gpu(input, data, scales, M: int, K: int, stream=None) -> None:
+    """BF16 [M, K] -> MXFP8 along K (each value widened exactly to FP32 first)."""
+    s = _stream(stream, input, data)
+    _check(lib().mpk_mxfp8_quantize_bf16(_addr(input), _addr(data), _addr(scales), M, K, s))
 
 
 def mxfp8_dequantize_bf16_gpu(data, scales, output, M: int, K: int, stream=None) -> None:

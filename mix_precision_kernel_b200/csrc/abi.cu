@@ -330,6 +330,26 @@ int mpk_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, float* outp
                      "dequantize launch");
 }
 
+int mpk_mxfp8_quantize_bf16(const void* input, uint8_t* data, uint8_t* scales, int M, int K, void* stream)
+{
+    if (M < 0 || K < 0) {
+        set_last_error("negative size M=%d K=%d", M, K);
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (M == 0 || K == 0) return MPK_SUCCESS;
+    if (!input || !data || !scales) {
+        set_last_error("null device pointer");
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (reinterpret_cast<uintptr_t>(input) & 1u) {
+        set_last_error("BF16 input must be 2-byte aligned");
+        return MPK_ERR_MISALIGNED;
+    }
+    if (int rc = check_arch()) return rc;
+    return from_cuda(launch_mxfp8_quantize_bf16(input, data, scales, M, K, (cudaStream_t)stream),
+                     "quantize-bf16 launch");
+}
+
 int mpk_mxfp8_dequantize_bf16(const uint8_t* data, const uint8_t* scales, void* output, int M, int K,
                               void* stream)
 {

@@ -73,8 +73,59 @@ mxfp8_quantize_flat_kernel(const float* __restrict__ in, uint8_t* __restrict__ d
     }
 }
 
+// BF16 source of the quantizer: each element widened exactly to FP32.
+__device__ __forceinline__ float load_elem(const float* p) { return *p; }
+__device__ __forceinline__ float load_elem(const uint16_t* p) { return __uint_as_float((uint32_t)*p << 16); }
+
+// BF16 [M][K] -> MXFP8 along K, flat path: lane l of a warp holds octet (8 BF16)
+// base + 32j + l for j < kQuantBf16U, so every load instruction reads 512
+// contiguous bytes; an MX block (4 octets) sits in 4 consecutive lanes.  Same
+// arithmetic as the FP32 quantizer on the widened values.
+constexpr int kQuantBf16U = 4;
+
 __global__ void __launch_bounds__(kCodecThreads)
-mxfp8_quantize_rowblock_kernel(const float* __restrict__ in, uint8_t* __restrict__ data,
+mxfp8_quantize_bf16_flat_kernel(const uint16_t* __restrict__ in, uint8_t* __restrict__ data,
+                                uint8_t* __restrict__ scales, int64_t n_octets)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const uint4* i8 = reinterpret_cast<const uint4*>(in);
+    for (int64_t base = warp * 32 * kQuantBf16U; base < n_octets; base += nwarps * 32 * kQuantBf16U) {
+        uint4 v[kQuantBf16U];
+#pragma unroll
+        for (int j = 0; j < kQuantBf16U; ++j) {
+            const int64_t o = base + 32 * j + lane;
+            v[j] = o < n_octets ? __ldcs(i8 + o) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int j = 0; j < kQuantBf16U; ++j) {
+            const int64_t o = base + 32 * j + lane;
+            const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+            float f[8];
+            float amax = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                f[2 * i] = __uint_as_float(w[i] << 16);
+                f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+                amax = fmaxf(amax, fmaxf(fabsf(f[2 * i]), fabsf(f[2 * i + 1])));
+            }
+            amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+            amax = fmaxf(amax, 0.0f);  // all-NaN block: amax 0, as the reference's max folded from 0
+            float inv;
+            const uint32_t s = mx_block_scale(amax, inv);
+            if (o < n_octets) {
+                __stcs(reinterpret_cast<uint2*>(data) + o, quantize8(f, inv));
+                if ((lane & 3) == 0) scales[o >> 2] = (uint8_t)s;
+            }
+        }
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kCodecThreads)
+mxfp8_quantize_rowblock_kernel(const T* __restrict__ in, uint8_t* __restrict__ data,
                                uint8_t* __restrict__ scales, int64_t M, int64_t K, int64_t nblk)
 {
     const int lane = threadIdx.x & 31;
@@ -83,7 +134,7 @@ mxfp8_quantize_rowblock_kernel(const float* __restrict__ in, uint8_t* __restrict
         const int64_t row = w / nblk, blk = w % nblk;
         const int64_t k = blk * 32 + lane;
         const bool valid = k < K;
-        const float x = valid ? in[row * K + k] : 0.0f;
+        const float x = valid ? load_elem(in + row * K + k) : 0.0f;
         float amax = fmaxf(0.0f, fabsf(x));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
@@ -295,8 +346,25 @@ cudaError_t launch_mxfp8_quantize(const float* in, uint8_t* data, uint8_t* scale
         mxfp8_quantize_flat_kernel<<<codec_grid(nf4 / kQuantU), kCodecThreads, 0, stream>>>(in, data, scales,
                                                                                          nf4);
     } else {
-        mxfp8_quantize_rowblock_kernel<<<codec_grid(M * nblk * 32), kCodecThreads, 0, stream>>>(
+        mxfp8_quantize_rowblock_kernel<float><<<codec_grid(M * nblk * 32), kCodecThreads, 0, stream>>>(
             in, data, scales, M, K, nblk);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mxfp8_quantize_bf16(const void* in, uint8_t* data, uint8_t* scales, int64_t M,
+                                       int64_t K, cudaStream_t stream)
+{
+    const int64_t nblk = (K + 31) / 32;
+    if (M == 0 || K == 0) return cudaSuccess;
+    const uint16_t* x = static_cast<const uint16_t*>(in);
+    if (K % 32 == 0 && aligned16(in) && (reinterpret_cast<uintptr_t>(data) & 7u) == 0) {
+        const int64_t no = M * K / 8;
+        mxfp8_quantize_bf16_flat_kernel<<<codec_grid(no / kQuantBf16U), kCodecThreads, 0, stream>>>(
+            x, data, scales, no);
+    } else {
+        mxfp8_quantize_rowblock_kernel<uint16_t><<<codec_grid(M * nblk * 32), kCodecThreads, 0, stream>>>(
+            x, data, scales, M, K, nblk);
     }
     return cudaGetLastError();
 }

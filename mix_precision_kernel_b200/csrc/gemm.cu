@@ -51,6 +51,10 @@ namespace gemm {
 
 constexpr int BM = 128;        // rows per CTA; the pair covers 2*BM
 constexpr int PAIR_M = 2 * BM;
+#ifndef MPK_PANEL_M
+#define MPK_PANEL_M 8
+#endif
+constexpr int kPanelM = MPK_PANEL_M;  // M tiles per raster panel (tile_coords)
 constexpr int BN = 256;        // output columns per tile (each CTA loads BN/2 of B)
 constexpr int BN_HALF = BN / 2;
 constexpr int BK = 64;
@@ -136,17 +140,28 @@ struct Params {
     int M, N, K;
     int nblkK, nblkN;
     int num_m_tiles, num_n_tiles, num_kb;
-    int vec_cd;  // C/D rows are 16-byte aligned: vector path for full 32-column chunks
+    int panel_m;  // M tiles per raster panel (tile_coords)
+    int vec_cd;   // C/D rows are 16-byte aligned: vector path for full 32-column chunks
 };
 
 // Wait-site ids reported in the device status word.
 enum { kSiteEmpty = 1, kSiteFullB = 2, kSiteFullA16 = 3, kSiteTmemEmpty = 4, kSiteTmemFull = 5,
        kSiteFullA8 = 6, kSiteEmptyA8 = 7, kSiteEmptyT = 8 };
 
+// Tile order for L2 reuse.  The tile grid is cut into panels of panel_m M tiles;
+// within a panel tiles go M fastest, then N.  The tiles in flight at once (one per
+// cluster, consecutive indices) then form a panel_m x (clusters / panel_m)
+// rectangle, so each A row band and each B column band they read is fetched from
+// HBM about once per wave and shared through L2 -- rather than once per tile, as
+// in a single row or column of 74 tiles (A or B re-read per tile column/row).
 __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& m0, int& n0)
 {
-    m0 = (tile % p.num_m_tiles) * PAIR_M;  // M fastest: consecutive clusters share a B column band
-    n0 = (tile / p.num_m_tiles) * BN;
+    const int per_panel = p.panel_m * p.num_n_tiles;
+    const int panel = tile / per_panel;
+    const int r = tile - panel * per_panel;
+    const int rows = min(p.panel_m, p.num_m_tiles - panel * p.panel_m);  // last panel may be short
+    m0 = (panel * p.panel_m + r % rows) * PAIR_M;
+    n0 = (r / rows) * BN;
 }
 
 // 16 scale bytes of one row starting at block index b0 (bytes past the row end
@@ -1011,6 +1026,10 @@ int gemm_setup(const uint8_t* A_scales, const void* B, int ldb, const uint8_t* C
     p.num_m_tiles = (M + PAIR_M - 1) / PAIR_M;
     p.num_n_tiles = (N + BN - 1) / BN;
     p.num_kb = (K + BK - 1) / BK;
+    // About sqrt(74 clusters) rows per panel keeps the in-flight rectangle square;
+    // up to 2 * kPanelM M tiles stay one panel (M fastest over all rows), which
+    // timed slightly better there.
+    p.panel_m = p.num_m_tiles <= 2 * kPanelM ? p.num_m_tiles : kPanelM;
     const bool al_c = C_data == nullptr || (reinterpret_cast<uintptr_t>(C_data) & 15u) == 0;
     const bool al_d = (reinterpret_cast<uintptr_t>(D_data) & 15u) == 0;
     p.vec_cd = (N % 16 == 0 && al_c && al_d) ? 1 : 0;

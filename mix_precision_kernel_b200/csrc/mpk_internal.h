@@ -17,6 +17,8 @@ cudaError_t launch_mxfp8_quantize(const float* in, uint8_t* data, uint8_t* scale
 cudaError_t launch_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, float* out,
                                     int64_t M, int64_t K, cudaStream_t stream);
 // MXFP8 [M][K] -> BF16 [M][K] (exact for scale bytes other than 1 and 2).
+cudaError_t launch_mxfp8_quantize_bf16(const void* in, uint8_t* data, uint8_t* scales, int64_t M,
+                                       int64_t K, cudaStream_t stream);
 cudaError_t launch_mxfp8_dequantize_bf16(const uint8_t* data, const uint8_t* scales, void* out,
                                          int64_t M, int64_t K, int64_t ld_out, cudaStream_t stream);
 // D = MXFP8(dequant(C)) along N (C may be null: D = MXFP8(0)).  The K == 0 GEMM.

@@ -206,3 +206,36 @@ def test_dequantize_bf16_all_codes_all_scales(mpk_lib, cuda, M, K, offset):
     got_nan = ((got & 0x7F80) == 0x7F80) & ((got & 0x7F) != 0)
     assert np.array_equal(nan, got_nan)
     assert np.array_equal(got[~nan], want[~nan])
+
+
+# ------------------------------ BF16 -> MXFP8 ------------------------------
+
+def _gpu_quantize_bf16(mpk, bits, offset=0):
+    import torch
+
+    M, K = bits.shape
+    src = torch.from_numpy(np.ascontiguousarray(bits).view(np.int16).reshape(-1)).to("cuda")
+    buf = torch.empty(src.numel() + offset, dtype=torch.int16, device="cuda")
+    buf[offset:].copy_(src)
+    d = torch.full((M, K), 0xEE, dtype=torch.uint8, device="cuda")
+    s = torch.full((M, (K + 31) // 32), 0xEE, dtype=torch.uint8, device="cuda")
+    mpk.mxfp8_quantize_bf16_gpu(buf.data_ptr() + 2 * offset, d, s, M, K)
+    torch.cuda.synchronize()
+    return to_host(d), to_host(s)
+
+
+@pytest.mark.parametrize("kind", ["normal", "bits"])
+@pytest.mark.parametrize("M,K,offset", [(256, 2048, 0), (64, 100, 0), (33, 256, 3), (7, 32, 0)])
+def test_quantize_bf16_bit_exact(mpk_lib, cuda, kind, M, K, offset):
+    """Equal to the FP32 quantizer of the oracle on the exactly widened values, for
+    N(0, 0.02^2) data and for arbitrary BF16 bit patterns (NaN, inf, subnormals),
+    on the flat path and on the general path (ragged K, unaligned input)."""
+    rng = np.random.default_rng(M * K + offset)
+    if kind == "normal":
+        bits = O.to_bf16_bits((rng.standard_normal((M, K)) * 0.02).astype(np.float32))
+    else:
+        bits = rng.integers(0, 1 << 16, (M, K), dtype=np.uint32).astype(np.uint16)
+        bits[0, :32] = 0x7FC0  # an all-NaN block
+    d, s = _gpu_quantize_bf16(mpk_lib, bits, offset)
+    wd, ws = O.quantize(O.bf16_bits_to_float(bits))
+    assert np.array_equal(d, wd) and np.array_equal(s, ws)
