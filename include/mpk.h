@@ -103,6 +103,45 @@ int mpk_gemm_mxfp8_bf16_noalloc(const uint8_t* A_data, const uint8_t* A_scales, 
                                 const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                                 uint8_t* D_scales, int M, int N, int K, void* stream);
 
+/* Fused GEMM + all-gather of D over NVLink, for an M-row slab of a GEMM whose D
+ * (M_total x N) every GPU keeps whole.  Computes this slab's D = A*B + C (A, C: the
+ * slab's M rows; B whole) and writes its rows as rows [row_offset, row_offset + M)
+ * of every destination: D_dest[0] / Ds_dest[0] is this GPU's full D / D scales, the
+ * others are the other GPUs' full buffers mapped into this process (peer pointers),
+ * written by the epilogue with peer stores while later tiles are still computing
+ * (each must be this GPU's memory or imported with mpk_ipc_import, and hold
+ * M_total rows; else MPK_ERR_INVALID_VALUE before any launch).
+ * The A workspace is the caller's, as for mpk_gemm_mxfp8_bf16_ws (must be non-NULL).
+ * The other GPUs' rows are in this GPU's buffer only after mpk_peer_barrier with the
+ * same epoch has completed on every GPU.  No counterpart in the reference (its path
+ * has no collective). */
+int mpk_gemm_mxfp8_bf16_gather(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
+                               const uint8_t* C_data, const uint8_t* C_scales, int M, int N, int K,
+                               int64_t row_offset, int M_total, uint8_t* const* D_dest,
+                               uint8_t* const* Ds_dest, int ndest, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* Stream-ordered barrier across `world` GPUs: flags[i] is GPU i's array of at least
+ * `world` uint32 slots (zeroed before first use, peer-mapped); every GPU calls it
+ * with the same epoch, which must increase by one from 1 on each use.  A GPU that
+ * does not arrive within the wait budget makes the others record site 0x17E in
+ * their device status word (mpk_device_status) and continue.  No counterpart in
+ * the reference. */
+int mpk_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t epoch, void* stream);
+
+/* Sharing a device buffer with the other processes of a node (CUDA IPC), for the
+ * destinations and flag arrays above.  mpk_ipc_export describes the allocation
+ * holding dev_ptr: a 64-byte handle, dev_ptr's offset in it and its size.
+ * mpk_ipc_import, called in another process with ITS OWN device current, maps that
+ * allocation for the current device (enabling peer access to the owner) and
+ * returns the address of the exported pointer; the gather and barrier entry points
+ * accept only pointers of the current device's allocations or of buffers imported
+ * on it.  mpk_ipc_close releases an import (reference counted).  No counterpart in
+ * the reference. */
+int mpk_ipc_export(const void* dev_ptr, void* handle, uint64_t* offset, uint64_t* alloc_bytes);
+int mpk_ipc_import(const void* handle, uint64_t offset, uint64_t alloc_bytes, void** dev_ptr);
+int mpk_ipc_close(void* dev_ptr);
+
 /* float [M][K] -> MXFP8 along K.  Replaces mxfp8_quantize_gpu (reference
  * include/mxfp8_utils.h:38-40, src/quantize/mxfp8_quantize.cu:82-88).  Bit-exact
  * with the reference's host and device quantizers.  Any K >= 1. */

@@ -27,7 +27,9 @@ __all__ = [
     "gemm_fp8_tensorcore", "mxfp8_quantize_gpu", "mxfp8_dequantize_gpu",
     "mxfp8_quantize_host", "mxfp8_dequantize_host",
     "gemm_fp8_tensorcore_ws", "gemm_workspace_size", "release_workspace_pool",
-    "mxfp8_dequantize_bf16_gpu", "mxfp8_quantize_bf16_gpu", "gemm_fp8_tensorcore_noalloc", "NOALLOC_SCRATCH_BYTES",
+    "mxfp8_dequantize_bf16_gpu", "mxfp8_quantize_bf16_gpu", "gemm_fp8_tensorcore_gather", "peer_barrier",
+    "ipc_export", "ipc_import", "ipc_close",
+    "gemm_fp8_tensorcore_noalloc", "NOALLOC_SCRATCH_BYTES",
     "gemm", "quantize", "dequantize", "device_status", "set_wait_timeout_ns", "wait_selftest",
     "MX_BLOCK", "nblk",
 ]
@@ -81,6 +83,12 @@ def lib() -> ctypes.CDLL:
             L.mpk_mxfp8_dequantize.argtypes = [vp, vp, vp, ci, ci, vp]
             L.mpk_mxfp8_dequantize_bf16.argtypes = [vp, vp, vp, ci, ci, vp]
             L.mpk_mxfp8_quantize_bf16.argtypes = [vp, vp, vp, ci, ci, vp]
+            L.mpk_gemm_mxfp8_bf16_gather.argtypes = [vp, vp, vp, vp, vp, ci, ci, ci, ctypes.c_int64, ci,
+                                                     vp, vp, ci, vp, ctypes.c_size_t, vp]
+            L.mpk_peer_barrier.argtypes = [vp, ci, ci, ctypes.c_uint32, vp]
+            L.mpk_ipc_export.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]
+            L.mpk_ipc_import.argtypes = [vp, ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]
+            L.mpk_ipc_close.argtypes = [vp]
             L.mpk_mxfp8_quantize_host.argtypes = [vp, u8p, u8p, ci, ci]
             L.mpk_mxfp8_dequantize_host.argtypes = [u8p, u8p, vp, ci, ci]
             L.mpk_device_status.argtypes = [ctypes.POINTER(ci)]
@@ -93,7 +101,8 @@ def lib() -> ctypes.CDLL:
             for f in ("mpk_gemm_mxfp8_bf16", "mpk_gemm_mxfp8_bf16_ws", "mpk_gemm_workspace_size",
                       "mpk_release_workspace_pool", "mpk_mxfp8_quantize", "mpk_mxfp8_dequantize",
                       "mpk_mxfp8_dequantize_bf16", "mpk_gemm_mxfp8_bf16_noalloc",
-                      "mpk_mxfp8_quantize_bf16",
+                      "mpk_mxfp8_quantize_bf16", "mpk_gemm_mxfp8_bf16_gather", "mpk_peer_barrier",
+                      "mpk_ipc_export", "mpk_ipc_import", "mpk_ipc_close",
                       "mpk_mxfp8_quantize_host", "mpk_mxfp8_dequantize_host", "mpk_device_status",
                       "mpk_set_wait_timeout_ns", "mpk_wait_selftest", "mpk_version"):
                 getattr(L, f).restype = ci
@@ -183,6 +192,48 @@ def gemm_fp8_tensorcore_noalloc(A_data, A_scales, B, C_data, C_scales, D_data, D
     s = _stream(stream, A_data, D_data)
     _check(lib().mpk_gemm_mxfp8_bf16_noalloc(_addr(A_data), _addr(A_scales), _addr(B), _addr(C_data),
                                              _addr(C_scales), _addr(D_data), _addr(D_scales), M, N, K, s))
+
+
+def gemm_fp8_tensorcore_gather(A_data, A_scales, B, C_data, C_scales, M: int, N: int, K: int,
+                               row_offset: int, M_total: int, D_dest, Ds_dest, workspace,
+                               stream=None) -> None:
+    """Fused GEMM + all-gather: this slab's D rows go to rows [row_offset, row_offset+M)
+    of every destination (device addresses; D_dest[0] is this GPU's full D).  The
+    other GPUs' rows are present after peer_barrier on every GPU."""
+    n = len(D_dest)
+    assert n == len(Ds_dest) and 1 <= n <= 8
+    dd = (ctypes.c_void_p * n)(*[_addr(x) for x in D_dest])
+    ds = (ctypes.c_void_p * n)(*[_addr(x) for x in Ds_dest])
+    s = _stream(stream, A_data)
+    nbytes = workspace.numel() * workspace.element_size()
+    _check(lib().mpk_gemm_mxfp8_bf16_gather(_addr(A_data), _addr(A_scales), _addr(B), _addr(C_data),
+                                            _addr(C_scales), M, N, K, row_offset, M_total, dd, ds, n,
+                                            _addr(workspace), nbytes, s))
+
+
+def peer_barrier(flags, rank: int, world: int, epoch: int, stream=None) -> None:
+    """Stream-ordered barrier over the GPUs' flag arrays (device addresses, rank order)."""
+    arr = (ctypes.c_void_p * world)(*[_addr(x) for x in flags])
+    _check(lib().mpk_peer_barrier(arr, rank, world, epoch, _stream(stream)))
+
+
+def ipc_export(t) -> tuple[bytes, int, int]:
+    """(handle, offset, allocation bytes) describing the device allocation of t."""
+    h = ctypes.create_string_buffer(64)
+    off, size = ctypes.c_uint64(0), ctypes.c_uint64(0)
+    _check(lib().mpk_ipc_export(_addr(t), h, ctypes.byref(off), ctypes.byref(size)))
+    return h.raw, off.value, size.value
+
+
+def ipc_import(handle: bytes, offset: int, alloc_bytes: int) -> int:
+    """Map another process's exported buffer for the current device; returns its address."""
+    p = ctypes.c_void_p(0)
+    _check(lib().mpk_ipc_import(ctypes.c_char_p(handle), offset, alloc_bytes, ctypes.byref(p)))
+    return p.value
+
+
+def ipc_close(addr: int) -> None:
+    _check(lib().mpk_ipc_close(addr))
 
 
 def release_workspace_pool() -> None:

@@ -19,7 +19,7 @@ INCLUDE = os.path.join(ROOT, "include")
 LIB_DIR = os.path.join(PKG, "_lib")
 LIB = os.path.join(LIB_DIR, "libmpk.so")
 
-SOURCES = ["abi.cu", "codec.cu", "gemm.cu"]
+SOURCES = ["abi.cu", "codec.cu", "gemm.cu", "peer.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-shared"]
 

@@ -297,6 +297,90 @@ int mpk_gemm_mxfp8_bf16_ws(const uint8_t* A_data, const uint8_t* A_scales, const
                                           M, N, K, workspace, (cudaStream_t)stream);
 }
 
+int mpk_gemm_mxfp8_bf16_gather(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
+                               const uint8_t* C_data, const uint8_t* C_scales, int M, int N, int K,
+                               int64_t row_offset, int M_total, uint8_t* const* D_dest,
+                               uint8_t* const* Ds_dest, int ndest, void* workspace,
+                               size_t workspace_bytes, void* stream)
+{
+    if (ndest < 1 || ndest > 8 || !D_dest || !Ds_dest) {
+        set_last_error("fused all-gather needs 1..8 destinations, got %d", ndest);
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (M < 0 || M_total < 0 || row_offset < 0 || row_offset + M > (int64_t)M_total) {
+        set_last_error("rows [%lld, %lld) do not fit in M_total=%d", (long long)row_offset,
+                       (long long)row_offset + M, M_total);
+        return MPK_ERR_INVALID_VALUE;
+    }
+    for (int d = 0; d < ndest; ++d) {
+        if (!D_dest[d] || !Ds_dest[d]) {
+            set_last_error("null destination %d", d);
+            return MPK_ERR_INVALID_VALUE;
+        }
+    }
+    bool done = false;
+    if (M > 0 && N > 0) {
+        // Every buffer the epilogue stores into must be mapped for this GPU and hold
+        // the whole M_total-row D (or its scales).
+        const size_t d_bytes = (size_t)M_total * (size_t)N, s_bytes = (size_t)M_total * (size_t)((N + 31) / 32);
+        for (int d = 0; d < ndest; ++d) {
+            if (int rc = check_store_target(D_dest[d], d_bytes, "a D destination")) return rc;
+            if (int rc = check_store_target(Ds_dest[d], s_bytes, "a D-scales destination")) return rc;
+        }
+    }
+    if (int rc = validate_gemm(A_data, A_scales, B_bf16, C_data, C_scales, D_dest[0], Ds_dest[0], M, N, K,
+                               done))
+        return rc;
+    if (done) return MPK_SUCCESS;
+    const cudaStream_t st = (cudaStream_t)stream;
+    const int64_t nblkN = (N + 31) / 32;
+    if (K == 0) {
+        for (int d = 0; d < ndest; ++d) {
+            if (int rc = from_cuda(launch_mxfp8_requantize(C_data, C_scales, D_dest[d] + row_offset * N,
+                                                           Ds_dest[d] + row_offset * nblkN, M, N, st),
+                                   "requantize launch"))
+                return rc;
+        }
+        return MPK_SUCCESS;
+    }
+    const size_t need = gemm_workspace_bytes(M, N, K, gemm_b_needs_copy(B_bf16, N));
+    if (!workspace || workspace_bytes < need) {
+        set_last_error("fused all-gather needs a workspace of %zu bytes, got %zu", need, workspace_bytes);
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (reinterpret_cast<uintptr_t>(workspace) & 15u) {
+        set_last_error("workspace must be 16-byte aligned");
+        return MPK_ERR_MISALIGNED;
+    }
+    GatherDest g;
+    std::memset(&g, 0, sizeof(g));
+    g.n_extra = ndest - 1;
+    g.row_offset = row_offset;
+    for (int d = 1; d < ndest; ++d) {
+        g.D_extra[d - 1] = D_dest[d];
+        g.Ds_extra[d - 1] = Ds_dest[d];
+    }
+    return launch_gemm_mxfp8_bf16_prepass(A_data, A_scales, B_bf16, C_data, C_scales, D_dest[0], Ds_dest[0],
+                                          M, N, K, workspace, st, &g);
+}
+
+int mpk_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t epoch, void* stream)
+{
+    if (!flags || world < 1 || world > 8 || rank < 0 || rank >= world || epoch == 0) {
+        set_last_error("peer barrier: bad arguments (rank %d, world %d, epoch %u)", rank, world, epoch);
+        return MPK_ERR_INVALID_VALUE;
+    }
+    for (int i = 0; i < world; ++i) {
+        if (!flags[i] || (reinterpret_cast<uintptr_t>(flags[i]) & 3u)) {
+            set_last_error("peer barrier: flag array %d is null or not 4-byte aligned", i);
+            return MPK_ERR_INVALID_VALUE;
+        }
+        if (int rc = check_store_target(flags[i], (size_t)world * 4u, "a barrier flag array")) return rc;
+    }
+    if (int rc = check_arch()) return rc;
+    return launch_peer_barrier(flags, rank, world, epoch, (cudaStream_t)stream);
+}
+
 int mpk_mxfp8_quantize(const float* input, uint8_t* data, uint8_t* scales, int M, int K, void* stream)
 {
     if (M < 0 || K < 0) {

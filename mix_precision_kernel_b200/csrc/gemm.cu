@@ -55,6 +55,7 @@ constexpr int PAIR_M = 2 * BM;
 #define MPK_PANEL_M 8
 #endif
 constexpr int kPanelM = MPK_PANEL_M;  // M tiles per raster panel (tile_coords)
+constexpr int kMaxGatherDest = 8;      // destinations of the fused all-gather (GPUs)
 constexpr int BN = 256;        // output columns per tile (each CTA loads BN/2 of B)
 constexpr int BN_HALF = BN / 2;
 constexpr int BK = 64;
@@ -142,6 +143,14 @@ struct Params {
     int num_m_tiles, num_n_tiles, num_kb;
     int panel_m;  // M tiles per raster panel (tile_coords)
     int vec_cd;   // C/D rows are 16-byte aligned: vector path for full 32-column chunks
+    // Fused all-gather (kernels instantiated with kGather only): D row r of this
+    // product is written as row row_offset + r of D_data and of every D_extra[i]
+    // (other GPUs' full-D buffers, reached by peer stores over NVLink), scales
+    // likewise.  C rows are read without the offset.
+    int n_extra;
+    int64_t row_offset;
+    uint8_t* D_extra[kMaxGatherDest - 1];
+    uint8_t* Ds_extra[kMaxGatherDest - 1];
 };
 
 // Wait-site ids reported in the device status word.
@@ -307,6 +316,7 @@ __device__ __forceinline__ uint32_t quantize_block32(float (&v)[32], uint4& c0, 
 // from TMEM itself (warp-collective; every lane calls this together), element-wise
 // C loads and D stores, columns past N kept out of the block amax.  Out of line to
 // keep the epilogue's hot code small.
+template <bool kGather>
 __device__ __noinline__ void epilogue_ragged_chunk(const Params& p, uint32_t taddr, uint32_t cscale,
                                                    bool has_c, bool row_ok, int64_t grow, int col0,
                                                    int valid)
@@ -327,16 +337,44 @@ __device__ __noinline__ void epilogue_ragged_chunk(const Params& p, uint32_t tad
     const uint32_t sd = quantize_block32(v, d0, d1);
     if (row_ok) {
         const uint32_t dw[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+        const int64_t drow = kGather ? grow + p.row_offset : grow;
+        const int ndest = kGather ? 1 + p.n_extra : 1;
+        for (int dst = 0; dst < ndest; ++dst) {
+            uint8_t* dd = dst == 0 ? p.D_data : p.D_extra[dst - 1];
+            uint8_t* ds = dst == 0 ? p.D_scales : p.Ds_extra[dst - 1];
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-            if (i < valid) p.D_data[grow * p.N + col0 + i] = (uint8_t)(dw[i >> 2] >> (8 * (i & 3)));
-        p.D_scales[grow * p.nblkN + col0 / 32] = (uint8_t)sd;
+            for (int i = 0; i < 32; ++i)
+                if (i < valid) dd[drow * p.N + col0 + i] = (uint8_t)(dw[i >> 2] >> (8 * (i & 3)));
+            ds[drow * p.nblkN + col0 / 32] = (uint8_t)sd;
+        }
+    }
+}
+
+// One full 32-column D chunk (two 16-byte stores) and its scale byte, to this GPU's
+// D and, in the fused all-gather, to every other destination.
+template <bool kGather>
+__device__ __forceinline__ void store_d_chunk(const Params& p, int64_t grow, int col0, uint4 d0, uint4 d1,
+                                              uint32_t sd)
+{
+    const int64_t drow = kGather ? grow + p.row_offset : grow;
+    uint4* dst = reinterpret_cast<uint4*>(p.D_data + drow * p.N + col0);
+    dst[0] = d0;
+    dst[1] = d1;
+    p.D_scales[drow * p.nblkN + col0 / 32] = (uint8_t)sd;
+    if (kGather) {
+        for (int i = 0; i < p.n_extra; ++i) {
+            uint4* pd = reinterpret_cast<uint4*>(p.D_extra[i] + drow * p.N + col0);
+            pd[0] = d0;
+            pd[1] = d1;
+            p.Ds_extra[i][drow * p.nblkN + col0 / 32] = (uint8_t)sd;
+        }
     }
 }
 
 // Epilogue of one CTA (4 warps, one thread per accumulator row): for every tile of
 // this cluster, wait for the accumulator, add the dequantized C, quantize D to MXFP8
 // along N and store it, then release the accumulator on rank 0's tempty barrier.
+template <bool kGather>
 __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base, uint32_t tfull0,
                                          uint32_t tempty_base, int cluster, int nclusters,
                                          uint32_t rank, int warp, int lane, volatile int* abort_flag)
@@ -417,14 +455,9 @@ __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base
                     }
                     uint4 d0, d1;
                     const uint32_t sd = quantize_block32(v, d0, d1);
-                    if (row_ok) {
-                        uint4* dst = reinterpret_cast<uint4*>(p.D_data + grow * p.N + col0);
-                        dst[0] = d0;
-                        dst[1] = d1;
-                        p.D_scales[grow * p.nblkN + col0 / 32] = (uint8_t)sd;
-                    }
+                    if (row_ok) store_d_chunk<kGather>(p, grow, col0, d0, d1, sd);
                 } else {
-                    epilogue_ragged_chunk(p, taddr, cs[ci], has_c, row_ok, grow, col0, valid);
+                    epilogue_ragged_chunk<kGather>(p, taddr, cs[ci], has_c, row_ok, grow, col0, valid);
                 }
             }
         }
@@ -698,7 +731,7 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
     } else {
         setmaxnreg_inc<kEpiRegs>();
         // -------------------------------- epilogue --------------------------------
-        run_epilogue(p, tmem_base, tfull(0), mapa_shared(tempty(0), 0), cluster, nclusters, rank, warp,
+        run_epilogue<false>(p, tmem_base, tfull(0), mapa_shared(tempty(0), 0), cluster, nclusters, rank, warp,
                      lane, abort_flag);
     }
 
@@ -746,6 +779,7 @@ constexpr int P_SMEM_BYTES = P_OFF_MISC + 16 + 1024;
 static_assert(P_SMEM_BYTES <= 232448, "exceeds the sm_100 per-block shared memory limit");
 constexpr uint32_t P_TX_BYTES = 2 * (A16_BYTES + B_BYTES);  // both CTAs' A and B per stage
 
+template <bool kGather>
 __global__ void __launch_bounds__(P_THREADS, 1)
 gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
                         const __grid_constant__ CUtensorMap tmap_b, const Params p)
@@ -876,7 +910,7 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
             mbar_wait(drain, 0, never_abort, nullptr, 0, kDrainTimeoutNs);
         }
     } else if (warp >= P_FIRST_EPI_WARP) {
-        run_epilogue(p, tmem_base, tfull(0), mapa_shared(tempty(0), 0), cluster, nclusters, rank, warp,
+        run_epilogue<kGather>(p, tmem_base, tfull(0), mapa_shared(tempty(0), 0), cluster, nclusters, rank, warp,
                      lane, abort_flag);
     }
 
@@ -906,6 +940,37 @@ __global__ void wait_selftest_kernel(int* status, uint64_t timeout_ns)
     }
     __syncthreads();
     if (threadIdx.x == 0) mbar_wait(smem_u32(&bar), 0, &abort_flag, status, 0x7F, timeout_ns);
+}
+
+// Cross-GPU barrier of the fused all-gather, one warp: lane t < world publishes
+// `epoch` into slot `rank` of GPU t's flag array (a peer store, after a system-scope
+// fence so that this GPU's earlier peer stores of D are visible first), then waits
+// until slot t of this GPU's own array holds `epoch` or later.  Each wait is
+// bounded: on expiry the site code 0x7E goes to the device status word and the
+// lane stops waiting.
+struct PeerFlags {
+    uint32_t* f[kMaxGatherDest];
+};
+
+__global__ void peer_barrier_kernel(PeerFlags flags, int rank, int world, uint32_t epoch, int* status,
+                                    uint64_t timeout_ns)
+{
+    const int t = threadIdx.x;
+    if (t >= world) return;
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(flags.f[t] + rank), "r"(epoch) : "memory");
+    const uint32_t* mine = flags.f[rank] + t;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+        if ((int32_t)(v - epoch) >= 0) break;
+        if (globaltimer_ns() - t0 > timeout_ns) {
+            atomicCAS(status, 0, kDevTimeoutBase + 0x7E);
+            break;
+        }
+        __nanosleep(2000);
+    }
 }
 
 }  // namespace gemm
@@ -1030,6 +1095,9 @@ int gemm_setup(const uint8_t* A_scales, const void* B, int ldb, const uint8_t* C
     // up to 2 * kPanelM M tiles stay one panel (M fastest over all rows), which
     // timed slightly better there.
     p.panel_m = p.num_m_tiles <= 2 * kPanelM ? p.num_m_tiles : kPanelM;
+    p.n_extra = 0;
+    p.row_offset = 0;
+    for (int i = 0; i < kMaxGatherDest - 1; ++i) p.D_extra[i] = p.Ds_extra[i] = nullptr;
     const bool al_c = C_data == nullptr || (reinterpret_cast<uintptr_t>(C_data) & 15u) == 0;
     const bool al_d = (reinterpret_cast<uintptr_t>(D_data) & 15u) == 0;
     p.vec_cd = (N % 16 == 0 && al_c && al_d) ? 1 : 0;
@@ -1078,6 +1146,7 @@ int ensure_smem_attr(const void* kernel, int bytes, bool* flag)
 }
 
 bool g_smem_attr_bf16a[64] = {};
+bool g_smem_attr_gather[64] = {};
 
 }  // namespace
 
@@ -1155,7 +1224,7 @@ int launch_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const
 int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scales, const void* B,
                                    const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                                    uint8_t* D_scales, int M, int N, int K, void* workspace,
-                                   cudaStream_t stream)
+                                   cudaStream_t stream, const GatherDest* gather)
 {
     using namespace gemm;
     int dev = 0;
@@ -1174,8 +1243,26 @@ int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scale
     if ((rc = encode_2d(enc, &tmap_a16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, workspace, (uint64_t)K,
                         (uint64_t)M, (uint64_t)lda * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
-    if ((rc = ensure_smem_attr((const void*)gemm_bf16a_mxfp8_kernel, P_SMEM_BYTES, &g_smem_attr_bf16a[dev])))
+    if (gather) {
+        if (gather->n_extra < 0 || gather->n_extra > kMaxGatherDest - 1) {
+            set_last_error("fused all-gather: %d extra destinations (at most %d)", gather->n_extra,
+                           kMaxGatherDest - 1);
+            return MPK_ERR_INVALID_VALUE;
+        }
+        p.n_extra = gather->n_extra;
+        p.row_offset = gather->row_offset;
+        for (int i = 0; i < gather->n_extra; ++i) {
+            p.D_extra[i] = gather->D_extra[i];
+            p.Ds_extra[i] = gather->Ds_extra[i];
+            if (reinterpret_cast<uintptr_t>(p.D_extra[i]) & 15u) p.vec_cd = 0;
+        }
+        if ((rc = ensure_smem_attr((const void*)gemm_bf16a_mxfp8_kernel<true>, P_SMEM_BYTES,
+                                   &g_smem_attr_gather[dev])))
+            return rc;
+    } else if ((rc = ensure_smem_attr((const void*)gemm_bf16a_mxfp8_kernel<false>, P_SMEM_BYTES,
+                                      &g_smem_attr_bf16a[dev]))) {
         return rc;
+    }
     if (copy_b) {
         const cudaError_t ce = cudaMemcpy2DAsync(b_copy, (size_t)ldb * 2, B, (size_t)N * 2, (size_t)N * 2,
                                                  (size_t)K, cudaMemcpyDeviceToDevice, stream);
@@ -1189,7 +1276,28 @@ int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scale
         set_last_error("A pre-pass launch failed: %s", cudaGetErrorString(e));
         return (int)e;
     }
-    return launch_pair_kernel(gemm_bf16a_mxfp8_kernel, P_SMEM_BYTES, P_THREADS, tmap_a16, tmap_b, p, stream);
+    if (gather)
+        return launch_pair_kernel(gemm_bf16a_mxfp8_kernel<true>, P_SMEM_BYTES, P_THREADS, tmap_a16, tmap_b, p,
+                                  stream);
+    return launch_pair_kernel(gemm_bf16a_mxfp8_kernel<false>, P_SMEM_BYTES, P_THREADS, tmap_a16, tmap_b, p,
+                              stream);
+}
+
+int launch_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t epoch, cudaStream_t stream)
+{
+    int dev = 0, rc = get_device(dev);
+    if (rc) return rc;
+    int* status = nullptr;
+    if ((rc = status_ptr(dev, &status))) return rc;
+    gemm::PeerFlags pf = {};
+    for (int i = 0; i < world; ++i) pf.f[i] = flags[i];
+    gemm::peer_barrier_kernel<<<1, 32, 0, stream>>>(pf, rank, world, epoch, status, wait_timeout_ns());
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_last_error("peer barrier launch failed: %s", cudaGetErrorString(e));
+        return (int)e;
+    }
+    return MPK_SUCCESS;
 }
 
 int read_and_clear_device_status(int* value)

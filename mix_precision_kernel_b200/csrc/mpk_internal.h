@@ -40,12 +40,27 @@ int check_onchip_gemm_shape(const uint8_t* A_data, const void* B, int N, int K);
 // multiple of 8 elements, and B is copied into the workspace with padded rows when
 // N % 8 != 0 or B is not 16-byte aligned (gemm_b_needs_copy).  `workspace` must be
 // 16-byte aligned and hold gemm_workspace_bytes(M, N, K, gemm_b_needs_copy(B, N)).
+// Extra destinations of the fused all-gather: D rows also go to row row_offset + r
+// of every D_extra[i] / Ds_extra[i] (other GPUs' full buffers), and row_offset
+// applies to D_data / D_scales too.
+struct GatherDest {
+    int n_extra;
+    int64_t row_offset;
+    uint8_t* D_extra[7];
+    uint8_t* Ds_extra[7];
+};
 bool gemm_b_needs_copy(const void* B, int N);
+// 0 if `bytes` bytes at ptr lie in memory the current device may store to (an
+// allocation of this device, or a buffer imported on it with mpk_ipc_import).
+int check_store_target(const void* ptr, size_t bytes, const char* what);
 size_t gemm_workspace_bytes(int M, int N, int K, bool copy_b);
 int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scales, const void* B,
                                    const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                                    uint8_t* D_scales, int M, int N, int K, void* workspace,
-                                   cudaStream_t stream);
+                                   cudaStream_t stream, const GatherDest* gather = nullptr);
+// Cross-GPU barrier over flag arrays (flags[i]: GPU i's array, at least `world`
+// uint32 slots, peer-accessible); bounded wait, expiry recorded in the status word.
+int launch_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t epoch, cudaStream_t stream);
 
 // Device-side status word of the GEMM kernels (gemm.cu): read and clear.
 int read_and_clear_device_status(int* value);

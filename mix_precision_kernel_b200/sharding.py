@@ -13,7 +13,13 @@ and C (and all of B), column j only on column j of B and C.  So
 Each rank runs the single-GPU kernel on its shard; no collective is on the
 compute path.  :func:`gather_d` is the optional all-gather of D (and its scales)
 onto every rank, through ``torch.distributed`` (NCCL over NVLink on GPUs, gloo on
-CPU).
+CPU).  :class:`GatherGemm` fuses that all-gather into the GEMM for M slabs: the
+kernel's epilogue stores each D tile into every GPU's full-D buffer (symmetric
+memory, peer stores over NVLink) while later tiles are still on the tensor cores,
+and a stream-ordered cross-GPU barrier ends the call.  The buffers are shared by
+CUDA IPC (``mpk_ipc_export`` / ``mpk_ipc_import``, opened with each rank's own
+device current), so every GPU's buffer is plain device memory reached by peer
+stores; no multicast object is created.
 """
 from __future__ import annotations
 
@@ -129,3 +135,84 @@ def sharded_gemm(A_data, A_scales, B, C_data, C_scales, shards: list[Shard], ran
     if c is not None:
         c, c_s = c.contiguous(), c_s.contiguous()
     return mpk.gemm(a, a_s, b, c, c_s, stream=stream)
+
+
+def _round_up(x: int, a: int) -> int:
+    return (x + a - 1) // a * a
+
+
+class GatherGemm:
+    """D = A*B + C for this rank's M slab, with D all-gathered inside the GEMM.
+
+    Every rank holds a full [M_total][N] D and its [M_total][ceil(N/32)] scales in
+    one device buffer, which every other rank maps by CUDA IPC.  A call runs, on
+    the current stream: a cross-GPU barrier (every rank has finished with the
+    previous call's D), the fused GEMM (this slab's D rows stored into all ranks'
+    buffers by the epilogue), and a second barrier (every rank's rows have landed).
+    The returned D views stay valid until the next call on any rank.  Collective:
+    all ranks construct it and call it in the same order.
+    """
+
+    def __init__(self, M_total: int, N: int, K: int, shards: list[Shard], group=None):
+        import torch
+        import torch.distributed as dist
+
+        import mix_precision_kernel_b200 as mpk
+
+        self.mpk = mpk
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("the fused all-gather supports up to 8 GPUs")
+        self.M_total, self.N, self.K = M_total, N, K
+        self.shard = shards[self.rank]
+        if self.shard.n0 != 0 or self.shard.n1 != N:
+            raise ValueError("GatherGemm shards by M rows only")
+        nblk_n = (N + MX_BLOCK - 1) // MX_BLOCK
+        self.off_s = _round_up(M_total * N, 256)
+        self.off_f = _round_up(self.off_s + M_total * nblk_n, 256)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.buf = torch.empty(self.off_f + 256, dtype=torch.uint8, device=dev)
+        self.buf[self.off_f:].zero_()
+        torch.cuda.synchronize()
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mpk.ipc_export(self.buf), group=group)
+        self.imported = [mpk.ipc_import(*everyone[r]) for r in range(self.world) if r != self.rank]
+        it = iter(self.imported)
+        ptrs = [self.buf.data_ptr() if r == self.rank else next(it) for r in range(self.world)]
+        self.group = group
+        order = [self.rank] + [r for r in range(self.world) if r != self.rank]
+        self.d_dest = [ptrs[r] for r in order]
+        self.ds_dest = [ptrs[r] + self.off_s for r in order]
+        self.flags = [p + self.off_f for p in ptrs]
+        self.epoch = 0
+        ws = mpk.gemm_workspace_size(self.shard.rows, N, K) + K * _round_up(N, 8) * 2 + 256
+        self.workspace = torch.empty(ws, dtype=torch.uint8, device=dev)
+        self.D = self.buf[: M_total * N].view(M_total, N)
+        self.Ds = self.buf[self.off_s: self.off_s + M_total * nblk_n].view(M_total, nblk_n)
+        dist.barrier(group)
+
+    def close(self) -> None:
+        """Unmap the other ranks' buffers.  Collective; no call may be in flight."""
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        dist.barrier(self.group)
+        for p in self.imported:
+            self.mpk.ipc_close(p)
+        self.imported = []
+        dist.barrier(self.group)
+
+    def barrier(self, stream=None) -> None:
+        self.epoch += 1
+        self.mpk.peer_barrier(self.flags, self.rank, self.world, self.epoch, stream)
+
+    def __call__(self, A_data, A_scales, B, C_data=None, C_scales=None, stream=None):
+        sh = self.shard
+        self.barrier(stream)
+        self.mpk.gemm_fp8_tensorcore_gather(A_data, A_scales, B, C_data, C_scales, sh.rows, self.N, self.K,
+                                            sh.m0, self.M_total, self.d_dest, self.ds_dest, self.workspace,
+                                            stream)
+        self.barrier(stream)
+        return self.D, self.Ds
