@@ -408,6 +408,9 @@ def run_gemm_arm(args, world, rank, local, dist):
     # Denominator: the burst cuBLAS figure, unless the clock record shows the power
     # cap acting during the timed region, in which case the sustained figure (the
     # same GEMM measured back to back under the cap).  Both fractions are reported.
+    gather = gather_measurement(args, world, rank, dist, mpk, L, M, N, K, Ad, As, B, Cd, Cs, D, Ds, stream) \
+        if world > 1 else None
+
     peaks, peak_src = load_peaks()
     burst = float(peaks["bf16_tflops"])
     sustained = float(peaks.get("bf16_tflops_sustained", burst))
@@ -457,7 +460,64 @@ def run_gemm_arm(args, world, rank, local, dist):
         "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
     }
     line["clocks"]["samples"] = clocks["samples"]
+    if gather is not None:
+        line["gather"] = gather
     return line
+
+
+def gather_measurement(args, world, rank, dist, mpk, L, M, N, K, Ad, As, B, Cd, Cs, D, Ds, stream):
+    """GEMM + all-gather of D onto every GPU, two ways, over the same M slabs: the
+    fused kernel (each D tile stored into every GPU's full-D buffer by the epilogue,
+    then a cross-GPU barrier) and the GEMM followed by NCCL all_gather_into_tensor
+    of D and its scales.  Times are max over ranks."""
+    import torch
+
+    from mix_precision_kernel_b200 import sharding as S
+
+    M_total = M * world
+    shards = S.plan(M_total, N, world, "m")
+    gg = S.GatherGemm(M_total, N, K, shards, None)
+    fullD = torch.empty((M_total, N), dtype=torch.uint8, device="cuda")
+    fullS = torch.empty((M_total, (N + 31) // 32), dtype=torch.uint8, device="cuda")
+    steps = max(5, min(args.steps, 50))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def fused():
+        gg(Ad, As, B, Cd, Cs)
+
+    def separate():
+        rc = L.mpk_gemm_mxfp8_bf16(Ad.data_ptr(), As.data_ptr(), B.data_ptr(), Cd.data_ptr(), Cs.data_ptr(),
+                                   D.data_ptr(), Ds.data_ptr(), M, N, K, stream.cuda_stream)
+        if rc:
+            raise mpk.MpkError(rc, L.mpk_last_error().decode())
+        dist.all_gather_into_tensor(fullD, D)
+        dist.all_gather_into_tensor(fullS, Ds)
+
+    out = {}
+    for name, fn in (("separate", separate), ("fused", fused)):
+        for _ in range(3):
+            fn()
+        barrier_sync(dist)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        barrier_sync(dist)
+        out[name] = max_over_ranks(dist, e0.elapsed_time(e1) / steps)
+    same = bool(torch.equal(gg.D, fullD)) and bool(torch.equal(gg.Ds, fullS))
+    ok = torch.tensor([1 if same else 0], device="cuda")
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    gg.close()
+    d_bytes = M * N + M * ((N + 31) // 32)
+    return {"what": "D = A*B + C on M slabs, then D and its scales on every GPU",
+            "fused_ms": round(out["fused"], 5), "separate_ms": round(out["separate"], 5),
+            "speedup": round(out["separate"] / out["fused"], 3),
+            "separate": "mpk GEMM + NCCL all_gather_into_tensor (D, scales)",
+            "fused": "GEMM epilogue stores every tile into all GPUs' full-D buffers (peer stores), "
+                     "cross-GPU barrier before and after",
+            "bytes_sent_per_gpu": d_bytes * (world - 1),
+            "nvlink_gbs_per_gpu_fused": round(d_bytes * (world - 1) / out["fused"] / 1e6, 1),
+            "results_identical": bool(ok.item()), "steps": steps}
 
 
 def run_codec_arm(args, world, rank, local, dist):

@@ -155,7 +155,7 @@ struct Params {
 
 // Wait-site ids reported in the device status word.
 enum { kSiteEmpty = 1, kSiteFullB = 2, kSiteFullA16 = 3, kSiteTmemEmpty = 4, kSiteTmemFull = 5,
-       kSiteFullA8 = 6, kSiteEmptyA8 = 7, kSiteEmptyT = 8 };
+       kSiteFullA8 = 6, kSiteEmptyA8 = 7, kSiteEmptyT = 8, kSiteEpiDone = 9, kSiteCopy = 10 };
 
 // Tile order for L2 reuse.  The tile grid is cut into panels of panel_m M tiles;
 // within a panel tiles go M fastest, then N.  The tiles in flight at once (one per
@@ -338,20 +338,16 @@ __device__ __noinline__ void epilogue_ragged_chunk(const Params& p, uint32_t tad
     if (row_ok) {
         const uint32_t dw[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
         const int64_t drow = kGather ? grow + p.row_offset : grow;
-        const int ndest = kGather ? 1 + p.n_extra : 1;
-        for (int dst = 0; dst < ndest; ++dst) {
-            uint8_t* dd = dst == 0 ? p.D_data : p.D_extra[dst - 1];
-            uint8_t* ds = dst == 0 ? p.D_scales : p.Ds_extra[dst - 1];
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (i < valid) dd[drow * p.N + col0 + i] = (uint8_t)(dw[i >> 2] >> (8 * (i & 3)));
-            ds[drow * p.nblkN + col0 / 32] = (uint8_t)sd;
-        }
+        for (int i = 0; i < 32; ++i)
+            if (i < valid) p.D_data[drow * p.N + col0 + i] = (uint8_t)(dw[i >> 2] >> (8 * (i & 3)));
+        p.D_scales[drow * p.nblkN + col0 / 32] = (uint8_t)sd;
     }
 }
 
-// One full 32-column D chunk (two 16-byte stores) and its scale byte, to this GPU's
-// D and, in the fused all-gather, to every other destination.
+// One full 32-column D chunk (two 16-byte stores) and its scale byte, into this
+// GPU's D (in the fused all-gather, at the slab's row offset of the full D; the
+// copy warps forward it to the other GPUs).
 template <bool kGather>
 __device__ __forceinline__ void store_d_chunk(const Params& p, int64_t grow, int col0, uint4 d0, uint4 d1,
                                               uint32_t sd)
@@ -361,13 +357,55 @@ __device__ __forceinline__ void store_d_chunk(const Params& p, int64_t grow, int
     dst[0] = d0;
     dst[1] = d1;
     p.D_scales[drow * p.nblkN + col0 / 32] = (uint8_t)sd;
-    if (kGather) {
-        for (int i = 0; i < p.n_extra; ++i) {
-            uint4* pd = reinterpret_cast<uint4*>(p.D_extra[i] + drow * p.N + col0);
-            pd[0] = d0;
-            pd[1] = d1;
-            p.Ds_extra[i][drow * p.nblkN + col0 / 32] = (uint8_t)sd;
+}
+
+// Fused all-gather, copy warps: forward one finished tile's D rows of this CTA
+// (128 rows x up to 256 columns, and their scale bytes) from this GPU's D to every
+// other destination.  Lanes of the copying warps take consecutive 16-byte pieces of
+// a row, so each store instruction writes whole row segments across NVLink;
+// kForwardU loads are in flight per lane before the stores.  Reads go through L2
+// (the tile was just written there).
+constexpr int kForwardU = 8;
+
+__device__ __forceinline__ void forward_tile(const Params& p, int64_t r0, int nrows, int n0, int ncols,
+                                             int t, int nthreads)
+{
+    const int64_t base_row = p.row_offset + r0;
+    const bool vec = p.vec_cd && (ncols % 16 == 0);
+    if (vec) {
+        const int per_row = ncols / 16;
+        const int units = nrows * per_row;
+        for (int u0 = t; u0 < units; u0 += kForwardU * nthreads) {
+            uint4 v[kForwardU];
+            int64_t off[kForwardU];
+#pragma unroll
+            for (int j = 0; j < kForwardU; ++j) {
+                const int u = u0 + j * nthreads;
+                off[j] = -1;
+                if (u < units) {
+                    off[j] = (base_row + u / per_row) * p.N + n0 + 16 * (u % per_row);
+                    v[j] = __ldcg(reinterpret_cast<const uint4*>(p.D_data + off[j]));
+                }
+            }
+            for (int i = 0; i < p.n_extra; ++i) {
+#pragma unroll
+                for (int j = 0; j < kForwardU; ++j)
+                    if (off[j] >= 0) *reinterpret_cast<uint4*>(p.D_extra[i] + off[j]) = v[j];
+            }
         }
+    } else {
+        const int units = nrows * ncols;
+        for (int u = t; u < units; u += nthreads) {
+            const int64_t off = (base_row + u / ncols) * p.N + n0 + u % ncols;
+            const uint8_t b = __ldcg(p.D_data + off);
+            for (int i = 0; i < p.n_extra; ++i) p.D_extra[i][off] = b;
+        }
+    }
+    const int nsc = (ncols + 31) / 32;
+    for (int u = t; u < nrows * nsc; u += nthreads) {
+        const int64_t off = (base_row + u / nsc) * p.nblkN + n0 / 32 + u % nsc;
+        const uint8_t b = __ldcg(p.D_scales + off);
+        for (int i = 0; i < p.n_extra; ++i) p.Ds_extra[i][off] = b;
     }
 }
 
@@ -377,7 +415,8 @@ __device__ __forceinline__ void store_d_chunk(const Params& p, int64_t grow, int
 template <bool kGather>
 __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base, uint32_t tfull0,
                                          uint32_t tempty_base, int cluster, int nclusters,
-                                         uint32_t rank, int warp, int lane, volatile int* abort_flag)
+                                         uint32_t rank, int warp, int lane, volatile int* abort_flag,
+                                         uint32_t epi_done = 0u, volatile int* tiles_done = nullptr)
 {
     const int num_tiles = p.num_m_tiles * p.num_n_tiles;
     auto tfull = [&](int a) { return tfull0 + 8u * a; };
@@ -465,6 +504,24 @@ __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(tempty_base + 8u * acc);
+        if (kGather && tiles_done != nullptr) {
+            // Publish "tile `it` of this CTA is in this GPU's D" to the copy warps:
+            // every epilogue thread arrives (release) after its stores; one thread
+            // waits for all 128 (acquire) and bumps the counter the copy warps poll.
+            mbar_arrive(epi_done);
+            bool ok = true;
+            if (quad == 0) {
+                if (lane == 0) {
+                    ok = mbar_wait(epi_done, (uint32_t)it & 1u, abort_flag, p.status, kSiteEpiDone, p.timeout_ns);
+                    if (ok) {
+                        __threadfence_block();
+                        *tiles_done = it + 1;
+                    }
+                }
+                ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;  // the warp leaves together
+            }
+            if (!ok) break;
+        }
     }
     }
 
@@ -772,8 +829,8 @@ constexpr int P_FIRST_EPI_WARP = 4;
 constexpr int P_OFF_B = 0;
 constexpr int P_OFF_A = P_OFF_B + P_STAGES * B_BYTES;
 constexpr int P_OFF_BAR = P_OFF_A + P_STAGES * A16_BYTES;
-// barriers: full[S], empty[S], tfull[2], tempty[2], drain
-constexpr int P_NUM_BARS = 2 * P_STAGES + 5;
+// barriers: full[S], empty[S], tfull[2], tempty[2], drain, epi_done
+constexpr int P_NUM_BARS = 2 * P_STAGES + 6;
 constexpr int P_OFF_MISC = P_OFF_BAR + P_NUM_BARS * 8;
 constexpr int P_SMEM_BYTES = P_OFF_MISC + 16 + 1024;
 static_assert(P_SMEM_BYTES <= 232448, "exceeds the sm_100 per-block shared memory limit");
@@ -793,9 +850,12 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
     auto tfull = [&](int a) { return bar0 + 8u * (2 * P_STAGES + a); };
     auto tempty = [&](int a) { return bar0 + 8u * (2 * P_STAGES + 2 + a); };
     const uint32_t drain = bar0 + 8u * (2 * P_STAGES + 4);
+    const uint32_t epi_done = bar0 + 8u * (2 * P_STAGES + 5);  // fused all-gather only
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + P_OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + P_OFF_MISC + 4);
     volatile int* never_abort = reinterpret_cast<volatile int*>(smem + P_OFF_MISC + 8);
+    volatile int* tiles_done = reinterpret_cast<volatile int*>(smem + P_OFF_MISC + 12);
+    const bool forward = kGather && p.n_extra > 0;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -814,8 +874,10 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
             mbar_init(tempty(a), 2 * kEpilogueWarps);
         }
         mbar_init(drain, 1);
+        mbar_init(epi_done, 4 * 32);
         *abort_flag = 0;
         *never_abort = 0;
+        *tiles_done = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -911,7 +973,35 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
         }
     } else if (warp >= P_FIRST_EPI_WARP) {
         run_epilogue<kGather>(p, tmem_base, tfull(0), mapa_shared(tempty(0), 0), cluster, nclusters, rank, warp,
-                     lane, abort_flag);
+                              lane, abort_flag, epi_done, forward ? tiles_done : nullptr);
+    } else if (forward) {
+        // ---------------- fused all-gather: copy warps 2 and 3 ----------------
+        // Forward every tile this CTA's epilogue has finished (tiles_done counts
+        // them, in this cluster's tile order) to the other GPUs' full-D buffers.
+        const int t = threadIdx.x - 64;
+        int it = 0;
+        for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
+            const uint64_t t0 = globaltimer_ns();
+            bool ok = true;
+            while (*tiles_done <= it) {
+                if (*abort_flag) { ok = false; break; }
+                if (globaltimer_ns() - t0 > p.timeout_ns) {
+                    *abort_flag = 1;
+                    atomicCAS(p.status, 0, kDevTimeoutBase + kSiteCopy);
+                    ok = false;
+                    break;
+                }
+                __nanosleep(256);
+            }
+            if (!ok) break;
+            __threadfence_block();
+            int m0, n0;
+            tile_coords(p, tile, m0, n0);
+            const int64_t r0 = (int64_t)m0 + BM * (int)rank;
+            const int nrows = (int)min((int64_t)BM, (int64_t)p.M - r0);
+            const int ncols = min(BN, p.N - n0);
+            if (nrows > 0) forward_tile(p, r0, nrows, n0, ncols, t, 64);
+        }
     }
 
     if (producer_aborted) {
