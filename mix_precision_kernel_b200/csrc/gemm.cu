@@ -365,7 +365,7 @@ __device__ __forceinline__ void store_d_chunk(const Params& p, int64_t grow, int
 // a row, so each store instruction writes whole row segments across NVLink;
 // kForwardU loads are in flight per lane before the stores.  Reads go through L2
 // (the tile was just written there).
-constexpr int kForwardU = 8;
+constexpr int kForwardU = 16;
 
 __device__ __forceinline__ void forward_tile(const Params& p, int64_t r0, int nrows, int n0, int ncols,
                                              int t, int nthreads)
