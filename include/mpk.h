@@ -19,9 +19,10 @@
  *   - every entry point returns a status code (0 = success) instead of calling
  *     exit() on failure; a detail message is available from mpk_last_error();
  *   - no call synchronizes the device; every launch is stream-ordered;
- *   - mpk_gemm_mxfp8_bf16 does not cudaMalloc/cudaFree per call: the M*K*2-byte
- *     workspace of its A pre-pass comes from a library-owned stream-ordered pool
- *     that stays reserved for reuse (mpk_release_workspace_pool returns it);
+ *   - mpk_gemm_mxfp8_bf16 does not cudaMalloc/cudaFree per call: the workspace of
+ *     its A pre-pass (about M*K*2 bytes, mpk_gemm_workspace_size) comes from a
+ *     library-owned stream-ordered pool that stays reserved for reuse
+ *     (mpk_release_workspace_pool returns it);
  *   - indexing is 64-bit.
  */
 #ifndef MPK_H_
