@@ -401,11 +401,23 @@ __device__ __forceinline__ void forward_tile(const Params& p, int64_t r0, int nr
             for (int i = 0; i < p.n_extra; ++i) p.D_extra[i][off] = b;
         }
     }
+    // Scale bytes: a full tile row has 8, one 8-byte piece when the scale rows are
+    // 8-byte aligned (one NVLink write instead of eight).
     const int nsc = (ncols + 31) / 32;
-    for (int u = t; u < nrows * nsc; u += nthreads) {
-        const int64_t off = (base_row + u / nsc) * p.nblkN + n0 / 32 + u % nsc;
-        const uint8_t b = __ldcg(p.D_scales + off);
-        for (int i = 0; i < p.n_extra; ++i) p.Ds_extra[i][off] = b;
+    bool sc_vec = nsc == 8 && p.nblkN % 8 == 0 && (reinterpret_cast<uintptr_t>(p.D_scales) & 7u) == 0;
+    for (int i = 0; i < p.n_extra; ++i) sc_vec = sc_vec && (reinterpret_cast<uintptr_t>(p.Ds_extra[i]) & 7u) == 0;
+    if (sc_vec) {
+        for (int r = t; r < nrows; r += nthreads) {
+            const int64_t off = (base_row + r) * p.nblkN + n0 / 32;
+            const uint2 v = __ldcg(reinterpret_cast<const uint2*>(p.D_scales + off));
+            for (int i = 0; i < p.n_extra; ++i) *reinterpret_cast<uint2*>(p.Ds_extra[i] + off) = v;
+        }
+    } else {
+        for (int u = t; u < nrows * nsc; u += nthreads) {
+            const int64_t off = (base_row + u / nsc) * p.nblkN + n0 / 32 + u % nsc;
+            const uint8_t b = __ldcg(p.D_scales + off);
+            for (int i = 0; i < p.n_extra; ++i) p.Ds_extra[i][off] = b;
+        }
     }
 }
 
