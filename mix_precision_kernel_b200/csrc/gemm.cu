@@ -38,6 +38,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -126,8 +127,10 @@ constexpr int SMEM_BYTES = SMEM_USED + 1024;  // slack for 1024-byte alignment
 static_assert(SMEM_BYTES <= 232448, "exceeds the sm_100 per-block shared memory limit");
 static_assert(A8_STAGES >= STAGES, "the transform's phase waits assume A8_STAGES >= STAGES");
 
-// Pair MMA: M = 256 across the two CTAs, N = 256, B MN-major.
+// Pair MMA: M = 256 across the two CTAs, N = 256 (N = 128 for split tail tiles),
+// B MN-major.
 constexpr uint32_t kIdesc = umma_idesc_bf16_f32(PAIR_M, BN, /*b_mn_major=*/true);
+constexpr uint32_t kIdescHalf = umma_idesc_bf16_f32(PAIR_M, BN / 2, /*b_mn_major=*/true);
 constexpr uint64_t kDrainTimeoutNs = 200000000ull;  // teardown waits: 0.2 s
 
 struct Params {
@@ -141,6 +144,9 @@ struct Params {
     int M, N, K;
     int nblkK, nblkN;
     int num_m_tiles, num_n_tiles, num_kb;
+    // Work items (item_coords): items below split_from are whole tiles in raster
+    // order; the remaining raster tiles are each cut into two 256 x 128 items.
+    int num_items, split_from;
     int panel_m;  // M tiles per raster panel (tile_coords)
     int vec_cd;   // C/D rows are 16-byte aligned: vector path for full 32-column chunks
     // Fused all-gather (kernels instantiated with kGather only): D row r of this
@@ -171,6 +177,21 @@ __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& m0, 
     const int rows = min(p.panel_m, p.num_m_tiles - panel * p.panel_m);  // last panel may be short
     m0 = (panel * p.panel_m + r % rows) * PAIR_M;
     n0 = (r / rows) * BN;
+}
+
+// Work item -> tile origin; returns the item's width (BN, or BN / 2 for the halves
+// of a split tail tile).  With 768 tiles on 74 clusters the eleventh wave would run
+// 28 tiles on 74 clusters; as 56 half tiles it takes half as long.
+__device__ __forceinline__ int item_coords(const Params& p, int item, int& m0, int& n0)
+{
+    if (item < p.split_from) {
+        tile_coords(p, item, m0, n0);
+        return BN;
+    }
+    const int j = item - p.split_from;
+    tile_coords(p, p.split_from + (j >> 1), m0, n0);
+    n0 += (j & 1) * (BN / 2);
+    return BN / 2;
 }
 
 // 16 scale bytes of one row starting at block index b0 (bytes past the row end
@@ -430,21 +451,20 @@ __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base
                                          uint32_t rank, int warp, int lane, volatile int* abort_flag,
                                          uint32_t epi_done = 0u, volatile int* tiles_done = nullptr)
 {
-    const int num_tiles = p.num_m_tiles * p.num_n_tiles;
     auto tfull = [&](int a) { return tfull0 + 8u * a; };
     const int quad = warp & 3;                 // TMEM lanes this warp may access
     const int r = quad * 32 + lane;            // accumulator row within this CTA's tile
     const bool has_c = p.C_data != nullptr;
     bool aborted = false;
     int it = 0;
-    for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
+    for (int item = cluster; item < p.num_items; item += nclusters, ++it) {
         int m0, n0;
-        tile_coords(p, tile, m0, n0);
+        const int bn = item_coords(p, item, m0, n0);
         const int acc = it & 1;
         const uint32_t acc_ph = (uint32_t)(it >> 1) & 1u;
         const int64_t grow = (int64_t)m0 + BM * (int)rank + r;
         const bool row_ok = grow < p.M;
-        const int nchunks = min(BN / 32, (p.N - n0 + 31) / 32);
+        const int nchunks = min(bn / 32, (p.N - n0 + 31) / 32);
         bool full_seen = false;
 #pragma unroll
         for (int c0 = 0; c0 < BN / 32; c0 += kCPrefetch) {
@@ -513,6 +533,10 @@ __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base
             }
         }
         if (aborted) break;
+        // An item with no columns inside N (the second half of a split tile at the
+        // right edge) still waits for its accumulator phase, so that phases pair up.
+        if (!full_seen && !mbar_wait(tfull(acc), acc_ph, abort_flag, p.status, kSiteTmemFull, p.timeout_ns))
+            break;
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(tempty_base + 8u * acc);
@@ -846,7 +870,7 @@ constexpr int P_NUM_BARS = 2 * P_STAGES + 6;
 constexpr int P_OFF_MISC = P_OFF_BAR + P_NUM_BARS * 8;
 constexpr int P_SMEM_BYTES = P_OFF_MISC + 16 + 1024;
 static_assert(P_SMEM_BYTES <= 232448, "exceeds the sm_100 per-block shared memory limit");
-constexpr uint32_t P_TX_BYTES = 2 * (A16_BYTES + B_BYTES);  // both CTAs' A and B per stage
+static_assert(BK * BN == B_BYTES, "per-stage B bytes of one CTA are BK * item width");
 
 template <bool kGather>
 __global__ void __launch_bounds__(P_THREADS, 1)
@@ -874,7 +898,6 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
     const uint32_t rank = cluster_ctarank();
     const int cluster = (int)cluster_id_x();
     const int nclusters = (int)nclusters_x();
-    const int num_tiles = p.num_m_tiles * p.num_n_tiles;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < P_STAGES; ++s) {
@@ -911,21 +934,22 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
             uint32_t ph = 0;
             int issued = 0;
             bool ok = true;
-            for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
+            for (int item = cluster; ok && item < p.num_items; item += nclusters) {
                 int m0, n0;
-                tile_coords(p, tile, m0, n0);
+                const int bn = item_coords(p, item, m0, n0);
                 const int row0 = m0 + BM * (int)rank;
-                const int col0 = n0 + BN_HALF * (int)rank;
+                const int col0 = n0 + (bn / 2) * (int)rank;
+                // both CTAs' A rows and B columns for one K-step
+                const uint32_t tx = 2u * (uint32_t)(A16_BYTES + BK * bn);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, p.status, kSiteEmpty, p.timeout_ns)) {
                         ok = false;
                         break;
                     }
-                    if (rank == 0) mbar_arrive_expect_tx(full(s), P_TX_BYTES);
+                    if (rank == 0) mbar_arrive_expect_tx(full(s), tx);
                     const uint32_t fb = mapa_shared(full(s), 0);
                     tma_load_2d_pair(sbase + P_OFF_A + s * A16_BYTES, &tmap_a16, fb, kb * BK, row0);
-#pragma unroll
-                    for (int j = 0; j < BN_HALF / 64; ++j)
+                    for (int j = 0; j < bn / 128; ++j)
                         tma_load_2d_pair(sbase + P_OFF_B + s * B_BYTES + j * B_BOX_BYTES, &tmap_b, fb,
                                          col0 + 64 * j, kb * BK);
                     ++issued;
@@ -950,7 +974,9 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
             uint32_t ph = 0;
             int it = 0;
             bool ok = true;
-            for (int tile = cluster; ok && tile < num_tiles; tile += nclusters, ++it) {
+            for (int item = cluster; ok && item < p.num_items; item += nclusters, ++it) {
+                int m0, n0;
+                const uint32_t idesc = item_coords(p, item, m0, n0) == BN ? kIdesc : kIdescHalf;
                 const int acc = it & 1;
                 const uint32_t acc_ph = (uint32_t)(it >> 1) & 1u;
                 if (!mbar_wait(tempty(acc), acc_ph ^ 1u, abort_flag, p.status, kSiteTmemEmpty,
@@ -972,7 +998,7 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
                     for (int k = 0; k < BK / UMMA_K; ++k) {
                         const uint64_t adesc = umma_smem_desc_sw128(a_addr + k * UMMA_K * 2, 16, 1024);
                         const uint64_t bdesc = umma_smem_desc_sw128(b_addr + k * UMMA_K * 128, B_BOX_BYTES, 1024);
-                        umma_bf16_pair(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0 ? 1u : 0u);
+                        umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
                     }
                     umma_commit_pair_mc(empty(s), 0x3);
                     if (++s == P_STAGES) { s = 0; ph ^= 1u; }
@@ -992,7 +1018,7 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
         // them, in this cluster's tile order) to the other GPUs' full-D buffers.
         const int t = threadIdx.x - 64;
         int it = 0;
-        for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
+        for (int item = cluster; item < p.num_items; item += nclusters, ++it) {
             const uint64_t t0 = globaltimer_ns();
             bool ok = true;
             while (*tiles_done <= it) {
@@ -1008,11 +1034,11 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
             if (!ok) break;
             __threadfence_block();
             int m0, n0;
-            tile_coords(p, tile, m0, n0);
+            const int bn = item_coords(p, item, m0, n0);
             const int64_t r0 = (int64_t)m0 + BM * (int)rank;
             const int nrows = (int)min((int64_t)BM, (int64_t)p.M - r0);
-            const int ncols = min(BN, p.N - n0);
-            if (nrows > 0) forward_tile(p, r0, nrows, n0, ncols, t, 64);
+            const int ncols = min(bn, p.N - n0);
+            if (nrows > 0 && ncols > 0) forward_tile(p, r0, nrows, n0, ncols, t, 64);
         }
     }
 
@@ -1193,6 +1219,7 @@ int gemm_setup(const uint8_t* A_scales, const void* B, int ldb, const uint8_t* C
     p.num_m_tiles = (M + PAIR_M - 1) / PAIR_M;
     p.num_n_tiles = (N + BN - 1) / BN;
     p.num_kb = (K + BK - 1) / BK;
+    p.num_items = p.split_from = p.num_m_tiles * p.num_n_tiles;
     // About sqrt(74 clusters) rows per panel keeps the in-flight rectangle square;
     // up to 2 * kPanelM M tiles stay one panel (M fastest over all rows), which
     // timed slightly better there.
@@ -1210,9 +1237,8 @@ template <typename Kernel>
 int launch_pair_kernel(Kernel kernel, int smem_bytes, int threads, const CUtensorMap& tmap_a,
                        const CUtensorMap& tmap_b, const gemm::Params& p, cudaStream_t stream)
 {
-    const int num_tiles = p.num_m_tiles * p.num_n_tiles;
     const int max_clusters = device_sm_count() / 2;
-    const int clusters = num_tiles < max_clusters ? num_tiles : max_clusters;
+    const int clusters = p.num_items < max_clusters ? p.num_items : max_clusters;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     cfg.blockDim = dim3(threads, 1, 1);
@@ -1371,6 +1397,16 @@ int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scale
         if (ce != cudaSuccess) {
             set_last_error("B row-padding copy failed: %s", cudaGetErrorString(ce));
             return (int)ce;
+        }
+    }
+    // Split the last wave's tiles in two when they would fill at most half of it.
+    {
+        const int tiles = p.num_m_tiles * p.num_n_tiles;
+        const int clusters = std::min(tiles, device_sm_count() / 2);
+        const int rem = tiles % clusters;
+        if (tiles > clusters && rem > 0 && 2 * rem <= clusters) {
+            p.split_from = tiles - rem;
+            p.num_items = tiles + rem;
         }
     }
     cudaError_t e = launch_mxfp8_dequantize_bf16(A_data, A_scales, workspace, M, K, lda, stream);

@@ -137,3 +137,24 @@ def test_pool_release_and_reuse(mpk_lib, cuda):
     mpk_lib.release_workspace_pool()
     mpk_lib.release_workspace_pool()
     assert np.array_equal(d0, d1) and np.array_equal(s0, s1)
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 5120, 256), (2048, 2816, 192)])
+def test_split_tail_tiles_match_onchip(mpk_lib, cuda, M, N, K):
+    """When the last wave would run at most half full, the pre-pass kernel cuts the
+    last raster tiles into 256 x 128 halves; D equals the on-chip kernel's (which
+    never splits) bit for bit."""
+    inp = O.make_gemm_inputs(M, N, K, seed=M + N)
+    d0, s0 = run_gemm(mpk_lib, inp)
+    d1, s1 = run_gemm(mpk_lib, inp, path="onchip")
+    assert np.array_equal(d0, d1) and np.array_equal(s0, s1)
+
+
+def test_split_tail_with_empty_half(mpk_lib, cuda):
+    """N = 2404: the last column of tiles has 100 columns, so the second half of each
+    split tile lies past N (no columns to store, accumulator phase still consumed)."""
+    M, N, K = 2048, 2404, 64
+    inp = O.make_gemm_inputs(M, N, K, seed=7)
+    Dd, Ds = run_gemm(mpk_lib, inp)
+    check_parity(Dd, Ds, O.gold_mx(inp), f"split tail {M}x{N}x{K}")
+    assert mpk_lib.device_status() == 0
