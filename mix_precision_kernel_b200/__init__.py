@@ -163,18 +163,26 @@ def gemm_workspace_size(M: int, N: int, K: int) -> int:
     return n.value
 
 
+def _nbytes(buf, nbytes):
+    """Size of a workspace given as a tensor, or as a raw address plus its size."""
+    if buf is None:
+        return 0
+    if isinstance(buf, int):
+        if nbytes is None:
+            raise ValueError("a workspace given as a raw address needs workspace_bytes")
+        return int(nbytes)
+    return buf.numel() * buf.element_size()
+
+
 def gemm_fp8_tensorcore_ws(A_data, A_scales, B, C_data, C_scales, D_data, D_scales,
-                           M: int, N: int, K: int, workspace, stream=None) -> None:
+                           M: int, N: int, K: int, workspace, stream=None,
+                           workspace_bytes: int | None = None) -> None:
     """gemm_fp8_tensorcore with the A operand dequantized into a caller workspace
-    (a uint8 CUDA tensor of at least gemm_workspace_size(M, N, K) bytes), or,
-    with workspace=None, converted on chip by the GEMM kernel itself."""
+    (a uint8 CUDA tensor of at least gemm_workspace_size(M, N, K) bytes, or a raw
+    device address with workspace_bytes), or, with workspace=None, converted on chip
+    by the GEMM kernel itself."""
     s = _stream(stream, A_data, D_data)
-    if workspace is None:
-        nbytes = 0
-    elif isinstance(workspace, int):
-        nbytes = 1 << 62
-    else:
-        nbytes = workspace.numel() * workspace.element_size()
+    nbytes = _nbytes(workspace, workspace_bytes)
     _check(lib().mpk_gemm_mxfp8_bf16_ws(_addr(A_data), _addr(A_scales), _addr(B), _addr(C_data),
                                         _addr(C_scales), _addr(D_data), _addr(D_scales), M, N, K,
                                         _addr(workspace), nbytes, s))
@@ -196,7 +204,7 @@ def gemm_fp8_tensorcore_noalloc(A_data, A_scales, B, C_data, C_scales, D_data, D
 
 def gemm_fp8_tensorcore_gather(A_data, A_scales, B, C_data, C_scales, M: int, N: int, K: int,
                                row_offset: int, M_total: int, D_dest, Ds_dest, workspace,
-                               stream=None) -> None:
+                               stream=None, workspace_bytes: int | None = None) -> None:
     """Fused GEMM + all-gather: this slab's D rows go to rows [row_offset, row_offset+M)
     of every destination (device addresses; D_dest[0] is this GPU's full D).  The
     other GPUs' rows are present after peer_barrier on every GPU."""
@@ -205,7 +213,7 @@ def gemm_fp8_tensorcore_gather(A_data, A_scales, B, C_data, C_scales, M: int, N:
     dd = (ctypes.c_void_p * n)(*[_addr(x) for x in D_dest])
     ds = (ctypes.c_void_p * n)(*[_addr(x) for x in Ds_dest])
     s = _stream(stream, A_data)
-    nbytes = workspace.numel() * workspace.element_size()
+    nbytes = _nbytes(workspace, workspace_bytes)
     _check(lib().mpk_gemm_mxfp8_bf16_gather(_addr(A_data), _addr(A_scales), _addr(B), _addr(C_data),
                                             _addr(C_scales), M, N, K, row_offset, M_total, dd, ds, n,
                                             _addr(workspace), nbytes, s))

@@ -123,3 +123,12 @@ def test_dropin_headers_compile(mpk_lib, tmp_path):
            f"-L{lib_dir}", "-lmpk", "-Xlinker", "-rpath", "-Xlinker", lib_dir, "-o", str(out)]
     subprocess.run(cmd, check=True, capture_output=True)
     assert out.exists()
+
+
+def test_raw_workspace_address_needs_a_size(mpk_lib):
+    """A workspace passed as a raw device address must come with its size, so the
+    library can check it (no GPU call is made: the check is in the binding)."""
+    import pytest
+
+    with pytest.raises(ValueError):
+        mpk_lib.gemm_fp8_tensorcore_ws(0, 0, 0, None, None, 0, 0, 16, 16, 16, 4096)

@@ -123,7 +123,8 @@ def test_ws_argument_checks(mpk_lib, cuda):
     assert e.value.status == mpk_lib.MPK_ERR_INVALID_VALUE
     big = torch.empty((need + 32,), dtype=torch.uint8, device="cuda")
     with pytest.raises(mpk_lib.MpkError) as e:
-        mpk_lib.gemm_fp8_tensorcore_ws(A, As, B, None, None, D, Ds, M, N, K, big[8:].data_ptr())
+        mpk_lib.gemm_fp8_tensorcore_ws(A, As, B, None, None, D, Ds, M, N, K, big[8:].data_ptr(),
+                                       workspace_bytes=need + 24)
     assert e.value.status == mpk_lib.MPK_ERR_MISALIGNED
 
 
