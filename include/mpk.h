@@ -54,10 +54,12 @@ enum {
  * from the library's pool on `stream` (rows padded to a multiple of 8 elements; B is
  * also copied there with padded rows when N % 8 != 0 or B is not 16-byte aligned),
  * then the tensor-core kernel streams both operands by TMA.  While `stream` is
- * being captured into a CUDA graph (or if the pool cannot supply the workspace) the
- * kernel that converts A on chip runs instead: it needs no workspace and gives a
- * bit-identical D, but needs K % 16 == 0, N % 8 == 0 and 16-byte aligned A_data and B
- * (else MPK_ERR_UNSUPPORTED / MPK_ERR_MISALIGNED). */
+ * being captured into a CUDA graph the workspace is a stream-ordered allocation
+ * (cudaMallocAsync), which the capture records as the graph's own allocation and
+ * free nodes.  If no workspace can be had, the kernel that converts A on chip runs
+ * instead: it needs no workspace and gives a bit-identical D, but needs K % 16 == 0,
+ * N % 8 == 0 and 16-byte aligned A_data and B (else MPK_ERR_UNSUPPORTED /
+ * MPK_ERR_MISALIGNED). */
 int mpk_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
                         const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                         uint8_t* D_scales, int M, int N, int K, void* stream);

@@ -222,27 +222,32 @@ int mpk_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const vo
         return from_cuda(launch_mxfp8_requantize(C_data, C_scales, D_data, D_scales, M, N, st),
                          "requantize launch");
     }
-    // Pre-pass path with the workspace taken from the pool on `stream`.  While the
-    // stream is being captured, or when the pool cannot supply the bytes, the
-    // in-kernel conversion runs instead: it needs no workspace and gives the same D.
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusActive;
+    // Pre-pass path.  Eager calls take the workspace from the library's pool on
+    // `stream`.  While `stream` is being captured into a CUDA graph, the workspace
+    // is a stream-ordered allocation of the device's default pool, which the
+    // capture turns into the graph's own memory allocation and free nodes.  If no
+    // workspace can be had (or the capture state cannot be read), the in-kernel
+    // conversion runs instead: it needs no workspace and gives the same D.
+    const size_t need = gemm_workspace_bytes(M, N, K, gemm_b_needs_copy(B_bf16, N));
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusInvalidated;
     if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) {
         cudaGetLastError();
-        cs = cudaStreamCaptureStatusActive;
+        cs = cudaStreamCaptureStatusInvalidated;
     }
+    void* ws = nullptr;
+    cudaError_t ae = cudaErrorNotReady;
     if (cs == cudaStreamCaptureStatusNone) {
-        if (cudaMemPool_t pool = workspace_pool(true)) {
-            void* ws = nullptr;
-            const size_t need = gemm_workspace_bytes(M, N, K, gemm_b_needs_copy(B_bf16, N));
-            if (cudaMallocFromPoolAsync(&ws, need, pool, st) == cudaSuccess) {
-                const int rc = launch_gemm_mxfp8_bf16_prepass(A_data, A_scales, B_bf16, C_data, C_scales,
-                                                              D_data, D_scales, M, N, K, ws, st);
-                const cudaError_t fe = cudaFreeAsync(ws, st);
-                return rc ? rc : from_cuda(fe, "workspace release");
-            }
-            cudaGetLastError();
-        }
+        if (cudaMemPool_t pool = workspace_pool(true)) ae = cudaMallocFromPoolAsync(&ws, need, pool, st);
+    } else if (cs == cudaStreamCaptureStatusActive) {
+        ae = cudaMallocAsync(&ws, need, st);
     }
+    if (ae == cudaSuccess) {
+        const int rc = launch_gemm_mxfp8_bf16_prepass(A_data, A_scales, B_bf16, C_data, C_scales, D_data,
+                                                      D_scales, M, N, K, ws, st);
+        const cudaError_t fe = cudaFreeAsync(ws, st);
+        return rc ? rc : from_cuda(fe, "workspace release");
+    }
+    if (ae != cudaErrorNotReady) cudaGetLastError();
     if (int rc = check_onchip_gemm_shape(A_data, B_bf16, N, K)) return rc;
     return launch_gemm_mxfp8_bf16(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales, M, N,
                                   K, st);

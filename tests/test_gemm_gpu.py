@@ -241,9 +241,9 @@ def test_any_alignment(mpk_lib, cuda, a_off, b_off, c_off, d_off):
 
 def test_stream_graph_capture_and_determinism(mpk_lib, cuda):
     """No launch path synchronizes, so both entry points capture into a CUDA
-    graph on a side stream.  Under capture the default entry point takes the
-    on-chip conversion kernel (no workspace to allocate); the workspace entry
-    point captures the pre-pass with the caller's buffer.  Replays give results
+    graph on a side stream.  Under capture the default entry point's workspace is
+    a stream-ordered allocation (graph memory nodes); the workspace entry point
+    captures the pre-pass with the caller's buffer.  Replays give results
     bit-identical to the eager (pooled pre-pass) call."""
     import torch
 
@@ -281,6 +281,31 @@ def test_stream_graph_capture_and_determinism(mpk_lib, cuda):
         torch.cuda.synchronize()
         assert np.array_equal(to_host(D), eager_d) and np.array_equal(to_host(S), eager_s)
     del g2
+
+
+def test_graph_capture_any_shape(mpk_lib, cuda):
+    """A shape outside the on-chip kernel's limits (N % 8 != 0) captures too: the
+    captured pre-pass path pads B and A in its graph-owned workspace."""
+    import torch
+
+    M, N, K = 192, 100, 72
+    inp = O.make_gemm_inputs(M, N, K, seed=17)
+    want_d, want_s = run_gemm(mpk_lib, inp)
+    A, As, B = to_dev(inp["A_data"]), to_dev(inp["A_scales"]), to_dev(inp["B_bf16"])
+    C, Cs = to_dev(inp["C_data"]), to_dev(inp["C_scales"])
+    D = torch.zeros((M, N), dtype=torch.uint8, device="cuda")
+    S = torch.zeros((M, (N + 31) // 32), dtype=torch.uint8, device="cuda")
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g, stream=s):
+        mpk_lib.gemm_fp8_tensorcore(A, As, B, C, Cs, D, S, M, N, K, s)
+    for _ in range(2):
+        D.zero_(); S.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert np.array_equal(to_host(D), want_d) and np.array_equal(to_host(S), want_s)
+    del g
 
 
 def test_wait_timeout_reports_status_without_fault(mpk_lib, cuda):
