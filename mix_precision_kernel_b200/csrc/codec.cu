@@ -288,6 +288,7 @@ __global__ void __launch_bounds__(kCodecThreads)
 mxfp8_dequantize_bf16_flat_kernel(const uint8_t* __restrict__ data, const uint8_t* __restrict__ scales,
                                   uint16_t* __restrict__ out, int64_t n_octets)
 {
+    allow_dependent_launch();
     const int lane = threadIdx.x & 31;
     const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -314,6 +315,7 @@ mxfp8_dequantize_bf16_elem_kernel(const uint8_t* __restrict__ data, const uint8_
                                   uint16_t* __restrict__ out, int64_t M, int64_t K, int64_t nblk,
                                   int64_t ld_out)
 {
+    allow_dependent_launch();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M * K; i += stride) {
         const int64_t row = i / K, k = i % K;

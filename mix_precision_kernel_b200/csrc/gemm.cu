@@ -930,6 +930,9 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
         if (lane == 0) {
             prefetch_tmap(&tmap_a16);
             prefetch_tmap(&tmap_b);
+            // The A pre-pass may still be running (programmatic dependent launch):
+            // BF16 A is read only after it has completed.
+            wait_for_prerequisite_grid();
             int s = 0;
             uint32_t ph = 0;
             int issued = 0;
@@ -1235,7 +1238,8 @@ int gemm_setup(const uint8_t* A_scales, const void* B, int ldb, const uint8_t* C
 
 template <typename Kernel>
 int launch_pair_kernel(Kernel kernel, int smem_bytes, int threads, const CUtensorMap& tmap_a,
-                       const CUtensorMap& tmap_b, const gemm::Params& p, cudaStream_t stream)
+                       const CUtensorMap& tmap_b, const gemm::Params& p, cudaStream_t stream,
+                       bool after_prepass = false)
 {
     const int max_clusters = device_sm_count() / 2;
     const int clusters = p.num_items < max_clusters ? p.num_items : max_clusters;
@@ -1244,13 +1248,17 @@ int launch_pair_kernel(Kernel kernel, int smem_bytes, int threads, const CUtenso
     cfg.blockDim = dim3(threads, 1, 1);
     cfg.dynamicSmemBytes = smem_bytes;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // After the A pre-pass: launch while it finishes (it allows dependents at its
+    // start); the producer waits for it before the first load of BF16 A.
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = after_prepass ? 2 : 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmap_a, tmap_b, p);
     if (e != cudaSuccess) {
         set_last_error("GEMM launch failed: %s", cudaGetErrorString(e));
@@ -1416,9 +1424,9 @@ int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scale
     }
     if (gather)
         return launch_pair_kernel(gemm_bf16a_mxfp8_kernel<true>, P_SMEM_BYTES, P_THREADS, tmap_a16, tmap_b, p,
-                                  stream);
+                                  stream, true);
     return launch_pair_kernel(gemm_bf16a_mxfp8_kernel<false>, P_SMEM_BYTES, P_THREADS, tmap_a16, tmap_b, p,
-                              stream);
+                              stream, true);
 }
 
 int launch_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t epoch, cudaStream_t stream)

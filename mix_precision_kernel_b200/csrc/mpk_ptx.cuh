@@ -20,6 +20,21 @@ namespace mpk {
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float e8m0_to_f32(uint32_t b) { return __uint_as_float(b << 23); }
 
+// Programmatic dependent launch.  A kernel that calls allow_dependent_launch lets
+// the next kernel on its stream, if launched with programmatic stream
+// serialization, start once all of this grid's blocks have called it; that
+// dependent kernel calls wait_for_prerequisite_grid before touching anything this
+// grid writes, which returns when this grid has completed and its memory is
+// visible.  Without the launch attribute both are no-ops.
+__device__ __forceinline__ void allow_dependent_launch()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void wait_for_prerequisite_grid()
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // Two E4M3 codes (low byte = first element) -> two floats, exact.
 __device__ __forceinline__ float2 e4m3x2_to_f32x2(uint32_t two_codes)
 {
