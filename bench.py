@@ -179,23 +179,32 @@ def max_over_ranks(dist, value: float) -> float:
 # ----------------------------------------------------------------------------
 # CPU baseline: the reference's own host implementation on a bounded row sample
 # ----------------------------------------------------------------------------
-def cpu_baseline(M, N, K, seed, budget_s: float, threads: int | None = None):
-    """Times gemm_reference_host + mxfp8_quantize_host (the reference's CPU path
-    for D = MXFP8(A*B + C)) on a row sample, one row slab per host thread.
-    Returns (TFLOP/s extrapolated to the full workload, description dict)."""
-    import numpy as np
+class CpuBaseline:
+    """gemm_reference_host + mxfp8_quantize_host (the reference's CPU path for
+    D = MXFP8(A*B + C)) timed on row samples, one row slab per host thread.  B is
+    drawn once; each sample draws fresh A and C rows.  Rows are independent, so the
+    throughput extrapolates linearly in M."""
 
-    import oracle as O
+    def __init__(self, M, N, K, seed, threads: int | None = None):
+        import numpy as np
 
-    threads = threads or O.default_threads()
-    kind = "reference" if O.ref_available() else "port"
-    rng = np.random.default_rng(seed)
-    B = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
-    B = O.bf16_bits_to_float(O.to_bf16_bits(B))
-    f32 = ctypes.POINTER(ctypes.c_float)
-    u8 = ctypes.POINTER(ctypes.c_uint8)
+        import oracle as O
 
-    def run_rows(nrows_per_thread: int) -> float:
+        self.O, self.np = O, np
+        self.M, self.N, self.K = M, N, K
+        self.threads = threads or O.default_threads()
+        self.kind = "reference" if O.ref_available() else "port"
+        rng = np.random.default_rng(seed)
+        B = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+        self.B = O.bf16_bits_to_float(O.to_bf16_bits(B))
+        self.rows = 1
+
+    def run_rows(self, nrows_per_thread: int, seed: int) -> float:
+        np, O, N, K, B = self.np, self.O, self.N, self.K, self.B
+        threads = self.threads
+        rng = np.random.default_rng(seed)
+        f32 = ctypes.POINTER(ctypes.c_float)
+        u8 = ctypes.POINTER(ctypes.c_uint8)
         A = (rng.standard_normal((threads * nrows_per_thread, K)) * 0.02).astype(np.float32)
         C = (rng.standard_normal((threads * nrows_per_thread, N)) * 0.02).astype(np.float32)
         A = O.dequantize(*O.quantize(A))
@@ -203,6 +212,7 @@ def cpu_baseline(M, N, K, seed, budget_s: float, threads: int | None = None):
         D = np.empty((A.shape[0], N), np.float32)
         Dd = np.empty((A.shape[0], N), np.uint8)
         Ds = np.empty((A.shape[0], (N + 31) // 32), np.uint8)
+        kind = self.kind
 
         def work(t):
             r0, r1 = t * nrows_per_thread, (t + 1) * nrows_per_thread
@@ -226,18 +236,27 @@ def cpu_baseline(M, N, K, seed, budget_s: float, threads: int | None = None):
             th.join()
         return time.perf_counter() - t0
 
-    # calibrate with one row per thread, then size the sample to the budget
-    t1 = run_rows(1)
-    rows = max(1, min(64, int(budget_s / max(t1, 1e-3))))
-    if rows > 1:
-        t1 = run_rows(rows)
-    flops = 2.0 * threads * rows * N * K
-    tflops = flops / t1 / 1e12
-    desc = {"value": tflops, "unit": "TFLOPS", "cores": threads, "kind": kind,
-            "sample": f"{threads * rows} rows x N={N} x K={K} ({threads} threads x {rows} rows, "
-                      f"{t1:.1f} s), extrapolated linearly in M to M={M}; "
-                      f"gemm_reference_host + mxfp8_quantize_host"}
-    return tflops, desc
+    def calibrate(self, budget_s: float, seed: int) -> None:
+        """Rows per thread so that one sample takes about budget_s."""
+        t1 = self.run_rows(1, seed)
+        self.rows = max(1, min(64, int(budget_s / max(t1, 1e-3))))
+
+    def sample(self, seed: int):
+        """One timed sample; returns (TFLOP/s extrapolated to M, description)."""
+        t = self.run_rows(self.rows, seed)
+        tflops = 2.0 * self.threads * self.rows * self.N * self.K / t / 1e12
+        desc = {"value": tflops, "unit": "TFLOPS", "cores": self.threads, "kind": self.kind,
+                "sample": f"{self.threads * self.rows} rows x N={self.N} x K={self.K} "
+                          f"({self.threads} threads x {self.rows} rows, {t:.2f} s), extrapolated "
+                          f"linearly in M to M={self.M}; gemm_reference_host + mxfp8_quantize_host"}
+        return tflops, desc
+
+
+def cpu_baseline(M, N, K, seed, budget_s: float, threads: int | None = None):
+    """One calibrated sample of the reference's CPU path (see CpuBaseline)."""
+    cb = CpuBaseline(M, N, K, seed, threads)
+    cb.calibrate(budget_s, seed + 1)
+    return cb.sample(seed + 2)
 
 
 def cpu_model() -> str:
@@ -592,10 +611,12 @@ def run_reference_arm(args, world, rank):
     # count so that the whole run stays within about two minutes of host work.
     budget = float(os.environ.get("MPK_REF_STEP_BUDGET_S", "2.0"))
     budget = max(0.05, min(budget, 120.0 / (args.steps + args.warmup)))
+    cb = CpuBaseline(M, N, K, seed)
+    cb.calibrate(budget, seed + 1)
     vals = []
     desc = None
     for i in range(args.warmup + args.steps):
-        v, desc = cpu_baseline(M, N, K, seed + i, budget)
+        v, desc = cb.sample(seed + 2 + i)
         if i >= args.warmup:
             vals.append(v)
     value = statistics.mean(vals)
