@@ -78,16 +78,78 @@ def load_traffic(kernel: str, workload: str):
 # ----------------------------------------------------------------------------
 # clocks during the timed region
 # ----------------------------------------------------------------------------
+def gpu_pci_id(cuda_index: int) -> str:
+    """PCI bus id of a CUDA device, which names the same GPU for nvidia-smi and NVML
+    whatever CUDA_VISIBLE_DEVICES or the CUDA device order is."""
+    import torch
+
+    pr = torch.cuda.get_device_properties(cuda_index)
+    return f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+
+
+class NvmlSampler:
+    """SM clock, clock-event reasons and power read through NVML every 10 ms on a
+    thread: finer than nvidia-smi's loop, so a short timed region still gets a
+    record.  Reading only; nothing is set."""
+    BITS = {"hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+            "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+            "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+            "sw_power_cap": "nvmlClocksEventReasonSwPowerCap"}
+
+    def __init__(self, pci_id: str, period_s: float = 0.01):
+        self.pci, self.period = pci_id, period_s
+        self.samples = []
+        self.stop_flag = threading.Event()
+        self.t = None
+
+    def start(self):
+        try:
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByPciBusId(self.pci)
+        except Exception:
+            return
+        self.nv, self.h = nv, h
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+
+    def _run(self):
+        nv, h = self.nv, self.h
+        while not self.stop_flag.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(h),
+                                     nv.nvmlDeviceGetPowerUsage(h) / 1000.0))
+            except Exception:
+                return
+            time.sleep(self.period)
+
+    def stop(self):
+        if self.t is None:
+            return None
+        self.stop_flag.set()
+        self.t.join(timeout=2)
+        if not self.samples:
+            return None
+        sm = [x[0] for x in self.samples]
+        reasons = sorted(n for n, a in self.BITS.items()
+                         if any(x[1] & getattr(self.nv, a) for x in self.samples))
+        return {"samples": len(sm), "sm_mhz_median": statistics.median(sm), "sm_mhz_min": min(sm),
+                "reasons": reasons, "power_w_max": round(max(x[2] for x in self.samples), 1)}
+
+
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int, period_ms: int = 50):
-        self.gpu = gpu_index
+    def __init__(self, gpu_id: str, period_ms: int = 50):
+        self.gpu = gpu_id
         self.period = period_ms
         self.proc = None
         self.lines = []
+        self.nvml = NvmlSampler(gpu_id)
 
     def start(self):
         try:
@@ -99,15 +161,17 @@ class ClockSampler:
             self.t.start()
         except OSError:
             self.proc = None
+        self.nvml.start()
 
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def stop(self):
+        nvml = self.nvml.stop()
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"],
-                    "samples": 0}
+                    "samples": 0, "nvml": nvml}
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -128,9 +192,11 @@ class ClockSampler:
             for n, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
+        if nvml:
+            reasons |= set(nvml["reasons"])
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "nvml": nvml}
 
 
 # ----------------------------------------------------------------------------
@@ -312,7 +378,7 @@ def run_gemm_arm(args, world, rank, local, dist):
     for _ in range(args.warmup):
         step()
     barrier_sync(dist)
-    sampler = ClockSampler(local)
+    sampler = ClockSampler(gpu_pci_id(local))
     sampler.start()
     time.sleep(0.3)  # let the sampler start before the timed region
     barrier_sync(dist)
@@ -479,6 +545,7 @@ def run_gemm_arm(args, world, rank, local, dist):
         "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
     }
     line["clocks"]["samples"] = clocks["samples"]
+    line["clocks"]["nvml_10ms"] = clocks.get("nvml")
     if gather is not None:
         line["gather"] = gather
     return line
