@@ -132,3 +132,33 @@ def test_raw_workspace_address_needs_a_size(mpk_lib):
 
     with pytest.raises(ValueError):
         mpk_lib.gemm_fp8_tensorcore_ws(0, 0, 0, None, None, 0, 0, 16, 16, 16, 4096)
+
+
+def test_collective_entry_points_validate_without_a_device(mpk_lib):
+    """The fused all-gather, the cross-GPU barrier and the IPC helpers refuse bad
+    arguments before touching a device."""
+    import ctypes
+
+    from mix_precision_kernel_b200 import MPK_ERR_INVALID_VALUE
+
+    L = mpk_lib.lib()
+    one = (ctypes.c_void_p * 1)(1 << 20)
+    nine = (ctypes.c_void_p * 9)(*([1 << 20] * 9))
+    # no destinations / too many destinations
+    assert L.mpk_gemm_mxfp8_bf16_gather(None, None, None, None, None, 8, 8, 16, 0, 8, one, one, 0,
+                                        None, 0, None) == MPK_ERR_INVALID_VALUE
+    assert L.mpk_gemm_mxfp8_bf16_gather(None, None, None, None, None, 8, 8, 16, 0, 8, nine, nine, 9,
+                                        None, 0, None) == MPK_ERR_INVALID_VALUE
+    # slab rows past the full D
+    assert L.mpk_gemm_mxfp8_bf16_gather(None, None, None, None, None, 8, 8, 16, 4, 8, one, one, 1,
+                                        None, 0, None) == MPK_ERR_INVALID_VALUE
+    # barrier: epoch 0, rank outside the world, world above 8
+    flags = (ctypes.c_void_p * 2)(1 << 20, 1 << 21)
+    assert L.mpk_peer_barrier(flags, 0, 2, 0, None) == MPK_ERR_INVALID_VALUE
+    assert L.mpk_peer_barrier(flags, 2, 2, 1, None) == MPK_ERR_INVALID_VALUE
+    assert L.mpk_peer_barrier(nine, 0, 9, 1, None) == MPK_ERR_INVALID_VALUE
+    # IPC: offset outside the allocation, closing a pointer that was never imported
+    handle = ctypes.create_string_buffer(64)
+    out = ctypes.c_void_p(0)
+    assert L.mpk_ipc_import(handle, 4096, 4096, ctypes.byref(out)) == MPK_ERR_INVALID_VALUE
+    assert L.mpk_ipc_close(1 << 20) == MPK_ERR_INVALID_VALUE
