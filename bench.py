@@ -120,23 +120,27 @@ class NvmlSampler:
             try:
                 self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
                                      nv.nvmlDeviceGetCurrentClocksEventReasons(h),
-                                     nv.nvmlDeviceGetPowerUsage(h) / 1000.0))
+                                     nv.nvmlDeviceGetPowerUsage(h) / 1000.0, time.monotonic()))
             except Exception:
                 return
             time.sleep(self.period)
 
-    def stop(self):
+    def stop(self, window=None):
+        """Statistics over the samples taken inside window = (t0, t1) (monotonic
+        seconds), or over all samples if none fall inside it."""
         if self.t is None:
             return None
         self.stop_flag.set()
         self.t.join(timeout=2)
         if not self.samples:
             return None
-        sm = [x[0] for x in self.samples]
-        reasons = sorted(n for n, a in self.BITS.items()
-                         if any(x[1] & getattr(self.nv, a) for x in self.samples))
-        return {"samples": len(sm), "sm_mhz_median": statistics.median(sm), "sm_mhz_min": min(sm),
-                "reasons": reasons, "power_w_max": round(max(x[2] for x in self.samples), 1)}
+        inside = [x for x in self.samples if window and window[0] <= x[3] <= window[1]]
+        sel = inside or self.samples
+        sm = [x[0] for x in sel]
+        reasons = sorted(n for n, a in self.BITS.items() if any(x[1] & getattr(self.nv, a) for x in sel))
+        return {"samples": len(sm), "in_timed_region": bool(inside), "sm_mhz_median": statistics.median(sm),
+                "sm_mhz_min": min(sm), "reasons": reasons,
+                "power_w_max": round(max(x[2] for x in sel), 1)}
 
 
 class ClockSampler:
@@ -150,6 +154,15 @@ class ClockSampler:
         self.proc = None
         self.lines = []
         self.nvml = NvmlSampler(gpu_id)
+        self.window = [None, None]
+
+    def begin(self):
+        """Marks the start of the timed region (host time, just before its launches)."""
+        self.window[0] = time.monotonic()
+
+    def end(self):
+        """Marks its end (host time, after the device synchronised)."""
+        self.window[1] = time.monotonic()
 
     def start(self):
         try:
@@ -165,10 +178,11 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
 
     def stop(self):
-        nvml = self.nvml.stop()
+        win = tuple(self.window) if None not in self.window else None
+        nvml = self.nvml.stop(win)
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"],
                     "samples": 0, "nvml": nvml}
@@ -180,7 +194,12 @@ class ClockSampler:
         self.t.join(timeout=2)
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        # nvidia-smi lines that arrived inside the timed region (plus one period of
+        # slack), or all of them when the region was shorter than the loop period
+        lines = [ln for t, ln in self.lines if win and win[0] <= t <= win[1] + self.period / 1000.0]
+        in_region = bool(lines)
+        lines = lines or [ln for _, ln in self.lines]
+        for ln in lines:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -196,7 +215,8 @@ class ClockSampler:
             reasons |= set(nvml["reasons"])
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm), "nvml": nvml}
+                "reasons": sorted(reasons), "samples": len(sm), "in_timed_region": in_region,
+                "nvml": nvml}
 
 
 # ----------------------------------------------------------------------------
@@ -383,11 +403,13 @@ def run_gemm_arm(args, world, rank, local, dist):
     time.sleep(0.3)  # let the sampler start before the timed region
     barrier_sync(dist)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler.begin()
     e0.record(stream)
     for _ in range(args.steps):
         step()
     e1.record(stream)
     barrier_sync(dist)
+    sampler.end()
     clocks = sampler.stop()
     ms = e0.elapsed_time(e1)
     assert mpk.device_status() == 0, "device wait expired"
@@ -545,6 +567,7 @@ def run_gemm_arm(args, world, rank, local, dist):
         "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
     }
     line["clocks"]["samples"] = clocks["samples"]
+    line["clocks"]["in_timed_region"] = clocks.get("in_timed_region")
     line["clocks"]["nvml_10ms"] = clocks.get("nvml")
     if gather is not None:
         line["gather"] = gather
