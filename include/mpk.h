@@ -106,22 +106,23 @@ int mpk_gemm_mxfp8_bf16_noalloc(const uint8_t* A_data, const uint8_t* A_scales, 
                                 const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                                 uint8_t* D_scales, int M, int N, int K, void* stream);
 
-/* Fused GEMM + all-gather of D over NVLink, for an M-row slab of a GEMM whose D
- * (M_total x N) every GPU keeps whole.  Computes this slab's D = A*B + C (A, C: the
- * slab's M rows; B whole) and writes its rows as rows [row_offset, row_offset + M)
- * of every destination: D_dest[0] / Ds_dest[0] is this GPU's full D / D scales, the
- * others are the other GPUs' full buffers mapped into this process (peer pointers),
- * written by the epilogue with peer stores while later tiles are still computing
- * (each must be this GPU's memory or imported with mpk_ipc_import, and hold
- * M_total rows; else MPK_ERR_INVALID_VALUE before any launch).
- * The A workspace is the caller's, as for mpk_gemm_mxfp8_bf16_ws (must be non-NULL).
- * The other GPUs' rows are in this GPU's buffer only after mpk_peer_barrier with the
- * same epoch has completed on every GPU.  No counterpart in the reference (its path
- * has no collective). */
+/* Fused GEMM + all-gather of D over NVLink, for one slab of a GEMM whose D
+ * (M_total x N_total) every GPU keeps whole: an M-row slab (A and C the slab's rows,
+ * B whole) or an N-column slab (A whole, B and C the slab's columns, col_offset a
+ * multiple of 32).  Computes the slab's D = A*B + C (M x N) and writes element (r, c)
+ * at (row_offset + r, col_offset + c) of every destination: D_dest[0] / Ds_dest[0] is
+ * this GPU's full D / D scales, the others are the other GPUs' full buffers mapped
+ * into this process (peer pointers), written while later tiles are still computing
+ * (each must be this GPU's memory or imported with mpk_ipc_import, and hold the
+ * M_total x N_total D; else MPK_ERR_INVALID_VALUE before any launch).  The A
+ * workspace is the caller's, as for mpk_gemm_mxfp8_bf16_ws (must be non-NULL).  The
+ * other GPUs' parts are in this GPU's buffer only after mpk_peer_barrier with the same
+ * epoch has completed on every GPU.  No counterpart in the reference (its path has
+ * no collective). */
 int mpk_gemm_mxfp8_bf16_gather(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
                                const uint8_t* C_data, const uint8_t* C_scales, int M, int N, int K,
-                               int64_t row_offset, int M_total, uint8_t* const* D_dest,
-                               uint8_t* const* Ds_dest, int ndest, void* workspace,
+                               int64_t row_offset, int64_t col_offset, int M_total, int N_total,
+                               uint8_t* const* D_dest, uint8_t* const* Ds_dest, int ndest, void* workspace,
                                size_t workspace_bytes, void* stream);
 
 /* Stream-ordered barrier across `world` GPUs: flags[i] is GPU i's array of at least

@@ -83,8 +83,9 @@ def lib() -> ctypes.CDLL:
             L.mpk_mxfp8_dequantize.argtypes = [vp, vp, vp, ci, ci, vp]
             L.mpk_mxfp8_dequantize_bf16.argtypes = [vp, vp, vp, ci, ci, vp]
             L.mpk_mxfp8_quantize_bf16.argtypes = [vp, vp, vp, ci, ci, vp]
-            L.mpk_gemm_mxfp8_bf16_gather.argtypes = [vp, vp, vp, vp, vp, ci, ci, ci, ctypes.c_int64, ci,
-                                                     vp, vp, ci, vp, ctypes.c_size_t, vp]
+            L.mpk_gemm_mxfp8_bf16_gather.argtypes = [vp, vp, vp, vp, vp, ci, ci, ci, ctypes.c_int64,
+                                                     ctypes.c_int64, ci, ci, vp, vp, ci, vp, ctypes.c_size_t,
+                                                     vp]
             L.mpk_peer_barrier.argtypes = [vp, ci, ci, ctypes.c_uint32, vp]
             L.mpk_ipc_export.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]
             L.mpk_ipc_import.argtypes = [vp, ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]
@@ -204,10 +205,12 @@ def gemm_fp8_tensorcore_noalloc(A_data, A_scales, B, C_data, C_scales, D_data, D
 
 def gemm_fp8_tensorcore_gather(A_data, A_scales, B, C_data, C_scales, M: int, N: int, K: int,
                                row_offset: int, M_total: int, D_dest, Ds_dest, workspace,
-                               stream=None, workspace_bytes: int | None = None) -> None:
-    """Fused GEMM + all-gather: this slab's D rows go to rows [row_offset, row_offset+M)
-    of every destination (device addresses; D_dest[0] is this GPU's full D).  The
-    other GPUs' rows are present after peer_barrier on every GPU."""
+                               stream=None, workspace_bytes: int | None = None,
+                               col_offset: int = 0, N_total: int | None = None) -> None:
+    """Fused GEMM + all-gather: element (r, c) of this slab's D goes to
+    (row_offset + r, col_offset + c) of every destination (device addresses;
+    D_dest[0] is this GPU's full M_total x N_total D).  The other GPUs' parts are
+    present after peer_barrier on every GPU."""
     n = len(D_dest)
     assert n == len(Ds_dest) and 1 <= n <= 8
     dd = (ctypes.c_void_p * n)(*[_addr(x) for x in D_dest])
@@ -215,7 +218,8 @@ def gemm_fp8_tensorcore_gather(A_data, A_scales, B, C_data, C_scales, M: int, N:
     s = _stream(stream, A_data)
     nbytes = _nbytes(workspace, workspace_bytes)
     _check(lib().mpk_gemm_mxfp8_bf16_gather(_addr(A_data), _addr(A_scales), _addr(B), _addr(C_data),
-                                            _addr(C_scales), M, N, K, row_offset, M_total, dd, ds, n,
+                                            _addr(C_scales), M, N, K, row_offset, col_offset, M_total,
+                                            N if N_total is None else N_total, dd, ds, n,
                                             _addr(workspace), nbytes, s))
 
 

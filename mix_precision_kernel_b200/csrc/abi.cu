@@ -304,17 +304,26 @@ int mpk_gemm_mxfp8_bf16_ws(const uint8_t* A_data, const uint8_t* A_scales, const
 
 int mpk_gemm_mxfp8_bf16_gather(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
                                const uint8_t* C_data, const uint8_t* C_scales, int M, int N, int K,
-                               int64_t row_offset, int M_total, uint8_t* const* D_dest,
-                               uint8_t* const* Ds_dest, int ndest, void* workspace,
+                               int64_t row_offset, int64_t col_offset, int M_total, int N_total,
+                               uint8_t* const* D_dest, uint8_t* const* Ds_dest, int ndest, void* workspace,
                                size_t workspace_bytes, void* stream)
 {
     if (ndest < 1 || ndest > 8 || !D_dest || !Ds_dest) {
         set_last_error("fused all-gather needs 1..8 destinations, got %d", ndest);
         return MPK_ERR_INVALID_VALUE;
     }
-    if (M < 0 || M_total < 0 || row_offset < 0 || row_offset + M > (int64_t)M_total) {
+    if (M < 0 || N < 0 || M_total < 0 || row_offset < 0 || row_offset + M > (int64_t)M_total) {
         set_last_error("rows [%lld, %lld) do not fit in M_total=%d", (long long)row_offset,
                        (long long)row_offset + M, M_total);
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (N_total < 0 || col_offset < 0 || col_offset % 32 != 0 || col_offset + N > (int64_t)N_total) {
+        set_last_error("columns [%lld, %lld) do not fit in N_total=%d or do not start on an MX block",
+                       (long long)col_offset, (long long)col_offset + N, N_total);
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (N != N_total && N % 32 != 0 && col_offset + N != N_total) {
+        set_last_error("a column slab must be a whole number of MX blocks unless it ends the row");
         return MPK_ERR_INVALID_VALUE;
     }
     for (int d = 0; d < ndest; ++d) {
@@ -326,8 +335,9 @@ int mpk_gemm_mxfp8_bf16_gather(const uint8_t* A_data, const uint8_t* A_scales, c
     bool done = false;
     if (M > 0 && N > 0) {
         // Every buffer the epilogue stores into must be mapped for this GPU and hold
-        // the whole M_total-row D (or its scales).
-        const size_t d_bytes = (size_t)M_total * (size_t)N, s_bytes = (size_t)M_total * (size_t)((N + 31) / 32);
+        // the whole M_total x N_total D (or its scales).
+        const size_t d_bytes = (size_t)M_total * (size_t)N_total;
+        const size_t s_bytes = (size_t)M_total * (size_t)((N_total + 31) / 32);
         for (int d = 0; d < ndest; ++d) {
             if (int rc = check_store_target(D_dest[d], d_bytes, "a D destination")) return rc;
             if (int rc = check_store_target(Ds_dest[d], s_bytes, "a D-scales destination")) return rc;
@@ -340,6 +350,10 @@ int mpk_gemm_mxfp8_bf16_gather(const uint8_t* A_data, const uint8_t* A_scales, c
     const cudaStream_t st = (cudaStream_t)stream;
     const int64_t nblkN = (N + 31) / 32;
     if (K == 0) {
+        if (N != N_total) {
+            set_last_error("K == 0 with a column slab is not supported by the fused all-gather");
+            return MPK_ERR_UNSUPPORTED;
+        }
         for (int d = 0; d < ndest; ++d) {
             if (int rc = from_cuda(launch_mxfp8_requantize(C_data, C_scales, D_dest[d] + row_offset * N,
                                                            Ds_dest[d] + row_offset * nblkN, M, N, st),
@@ -361,6 +375,8 @@ int mpk_gemm_mxfp8_bf16_gather(const uint8_t* A_data, const uint8_t* A_scales, c
     std::memset(&g, 0, sizeof(g));
     g.n_extra = ndest - 1;
     g.row_offset = row_offset;
+    g.col_offset = col_offset;
+    g.ldd = N_total;
     for (int d = 1; d < ndest; ++d) {
         g.D_extra[d - 1] = D_dest[d];
         g.Ds_extra[d - 1] = Ds_dest[d];

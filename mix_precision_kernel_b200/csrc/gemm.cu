@@ -149,12 +149,13 @@ struct Params {
     int num_items, split_from;
     int panel_m;  // M tiles per raster panel (tile_coords)
     int vec_cd;   // C/D rows are 16-byte aligned: vector path for full 32-column chunks
-    // Fused all-gather (kernels instantiated with kGather only): D row r of this
-    // product is written as row row_offset + r of D_data and of every D_extra[i]
-    // (other GPUs' full-D buffers, reached by peer stores over NVLink), scales
-    // likewise.  C rows are read without the offset.
+    // Fused all-gather (kernels instantiated with kGather only): element (r, c) of
+    // this product is written at (row_offset + r, col_offset + c) of D_data and of
+    // every D_extra[i] (other GPUs' full-D buffers, reached by peer stores over
+    // NVLink), whose rows are ldd bytes apart (scale rows lds apart); col_offset is
+    // a multiple of 32.  C is read at (r, c) of this product.
     int n_extra;
-    int64_t row_offset;
+    int64_t row_offset, col_offset, ldd, lds;
     uint8_t* D_extra[kMaxGatherDest - 1];
     uint8_t* Ds_extra[kMaxGatherDest - 1];
 };
@@ -358,11 +359,13 @@ __device__ __noinline__ void epilogue_ragged_chunk(const Params& p, uint32_t tad
     const uint32_t sd = quantize_block32(v, d0, d1);
     if (row_ok) {
         const uint32_t dw[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
-        const int64_t drow = kGather ? grow + p.row_offset : grow;
+        const int64_t doff = kGather ? (grow + p.row_offset) * p.ldd + p.col_offset + col0 : grow * p.N + col0;
+        const int64_t soff = kGather ? (grow + p.row_offset) * p.lds + (p.col_offset + col0) / 32
+                                     : grow * p.nblkN + col0 / 32;
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-            if (i < valid) p.D_data[drow * p.N + col0 + i] = (uint8_t)(dw[i >> 2] >> (8 * (i & 3)));
-        p.D_scales[drow * p.nblkN + col0 / 32] = (uint8_t)sd;
+            if (i < valid) p.D_data[doff + i] = (uint8_t)(dw[i >> 2] >> (8 * (i & 3)));
+        p.D_scales[soff] = (uint8_t)sd;
     }
 }
 
@@ -373,11 +376,13 @@ template <bool kGather>
 __device__ __forceinline__ void store_d_chunk(const Params& p, int64_t grow, int col0, uint4 d0, uint4 d1,
                                               uint32_t sd)
 {
-    const int64_t drow = kGather ? grow + p.row_offset : grow;
-    uint4* dst = reinterpret_cast<uint4*>(p.D_data + drow * p.N + col0);
+    const int64_t doff = kGather ? (grow + p.row_offset) * p.ldd + p.col_offset + col0 : grow * p.N + col0;
+    const int64_t soff = kGather ? (grow + p.row_offset) * p.lds + (p.col_offset + col0) / 32
+                                 : grow * p.nblkN + col0 / 32;
+    uint4* dst = reinterpret_cast<uint4*>(p.D_data + doff);
     dst[0] = d0;
     dst[1] = d1;
-    p.D_scales[drow * p.nblkN + col0 / 32] = (uint8_t)sd;
+    p.D_scales[soff] = (uint8_t)sd;
 }
 
 // Fused all-gather, copy warps: forward one finished tile's D rows of this CTA
@@ -392,6 +397,7 @@ __device__ __forceinline__ void forward_tile(const Params& p, int64_t r0, int nr
                                              int t, int nthreads)
 {
     const int64_t base_row = p.row_offset + r0;
+    const int64_t c0 = p.col_offset + n0;  // the tile's first column in the full D
     const bool vec = p.vec_cd && (ncols % 16 == 0);
     if (vec) {
         const int per_row = ncols / 16;
@@ -404,7 +410,7 @@ __device__ __forceinline__ void forward_tile(const Params& p, int64_t r0, int nr
                 const int u = u0 + j * nthreads;
                 off[j] = -1;
                 if (u < units) {
-                    off[j] = (base_row + u / per_row) * p.N + n0 + 16 * (u % per_row);
+                    off[j] = (base_row + u / per_row) * p.ldd + c0 + 16 * (u % per_row);
                     v[j] = __ldcg(reinterpret_cast<const uint4*>(p.D_data + off[j]));
                 }
             }
@@ -417,7 +423,7 @@ __device__ __forceinline__ void forward_tile(const Params& p, int64_t r0, int nr
     } else {
         const int units = nrows * ncols;
         for (int u = t; u < units; u += nthreads) {
-            const int64_t off = (base_row + u / ncols) * p.N + n0 + u % ncols;
+            const int64_t off = (base_row + u / ncols) * p.ldd + c0 + u % ncols;
             const uint8_t b = __ldcg(p.D_data + off);
             for (int i = 0; i < p.n_extra; ++i) p.D_extra[i][off] = b;
         }
@@ -425,17 +431,18 @@ __device__ __forceinline__ void forward_tile(const Params& p, int64_t r0, int nr
     // Scale bytes: a full tile row has 8, one 8-byte piece when the scale rows are
     // 8-byte aligned (one NVLink write instead of eight).
     const int nsc = (ncols + 31) / 32;
-    bool sc_vec = nsc == 8 && p.nblkN % 8 == 0 && (reinterpret_cast<uintptr_t>(p.D_scales) & 7u) == 0;
+    bool sc_vec = nsc == 8 && p.lds % 8 == 0 && (c0 / 32) % 8 == 0 &&
+                  (reinterpret_cast<uintptr_t>(p.D_scales) & 7u) == 0;
     for (int i = 0; i < p.n_extra; ++i) sc_vec = sc_vec && (reinterpret_cast<uintptr_t>(p.Ds_extra[i]) & 7u) == 0;
     if (sc_vec) {
         for (int r = t; r < nrows; r += nthreads) {
-            const int64_t off = (base_row + r) * p.nblkN + n0 / 32;
+            const int64_t off = (base_row + r) * p.lds + c0 / 32;
             const uint2 v = __ldcg(reinterpret_cast<const uint2*>(p.D_scales + off));
             for (int i = 0; i < p.n_extra; ++i) *reinterpret_cast<uint2*>(p.Ds_extra[i] + off) = v;
         }
     } else {
         for (int u = t; u < nrows * nsc; u += nthreads) {
-            const int64_t off = (base_row + u / nsc) * p.nblkN + n0 / 32 + u % nsc;
+            const int64_t off = (base_row + u / nsc) * p.lds + c0 / 32 + u % nsc;
             const uint8_t b = __ldcg(p.D_scales + off);
             for (int i = 0; i < p.n_extra; ++i) p.Ds_extra[i][off] = b;
         }
@@ -1228,7 +1235,9 @@ int gemm_setup(const uint8_t* A_scales, const void* B, int ldb, const uint8_t* C
     // timed slightly better there.
     p.panel_m = p.num_m_tiles <= 2 * kPanelM ? p.num_m_tiles : kPanelM;
     p.n_extra = 0;
-    p.row_offset = 0;
+    p.row_offset = p.col_offset = 0;
+    p.ldd = N;
+    p.lds = p.nblkN;
     for (int i = 0; i < kMaxGatherDest - 1; ++i) p.D_extra[i] = p.Ds_extra[i] = nullptr;
     const bool al_c = C_data == nullptr || (reinterpret_cast<uintptr_t>(C_data) & 15u) == 0;
     const bool al_d = (reinterpret_cast<uintptr_t>(D_data) & 15u) == 0;
@@ -1387,6 +1396,10 @@ int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scale
         }
         p.n_extra = gather->n_extra;
         p.row_offset = gather->row_offset;
+        p.col_offset = gather->col_offset;
+        p.ldd = gather->ldd;
+        p.lds = (gather->ldd + 31) / 32;
+        if (p.ldd % 16 != 0 || p.col_offset % 16 != 0) p.vec_cd = 0;
         for (int i = 0; i < gather->n_extra; ++i) {
             p.D_extra[i] = gather->D_extra[i];
             p.Ds_extra[i] = gather->Ds_extra[i];

@@ -40,12 +40,12 @@ int check_onchip_gemm_shape(const uint8_t* A_data, const void* B, int N, int K);
 // multiple of 8 elements, and B is copied into the workspace with padded rows when
 // N % 8 != 0 or B is not 16-byte aligned (gemm_b_needs_copy).  `workspace` must be
 // 16-byte aligned and hold gemm_workspace_bytes(M, N, K, gemm_b_needs_copy(B, N)).
-// Extra destinations of the fused all-gather: D rows also go to row row_offset + r
-// of every D_extra[i] / Ds_extra[i] (other GPUs' full buffers), and row_offset
-// applies to D_data / D_scales too.
+// Extra destinations of the fused all-gather: element (r, c) of the product goes to
+// (row_offset + r, col_offset + c) of D_data and of every D_extra[i] (other GPUs' full
+// buffers), rows ldd bytes apart; col_offset is a multiple of 32.
 struct GatherDest {
     int n_extra;
-    int64_t row_offset;
+    int64_t row_offset, col_offset, ldd;
     uint8_t* D_extra[7];
     uint8_t* Ds_extra[7];
 };

@@ -142,7 +142,7 @@ def _round_up(x: int, a: int) -> int:
 
 
 class GatherGemm:
-    """D = A*B + C for this rank's M slab, with D all-gathered inside the GEMM.
+    """D = A*B + C for this rank's M or N slab, with D all-gathered inside the GEMM.
 
     Every rank holds a full [M_total][N] D and its [M_total][ceil(N/32)] scales in
     one device buffer, which every other rank maps by CUDA IPC.  A call runs, on
@@ -165,9 +165,13 @@ class GatherGemm:
         if self.world > 8:
             raise ValueError("the fused all-gather supports up to 8 GPUs")
         self.M_total, self.N, self.K = M_total, N, K
-        self.shard = shards[self.rank]
-        if self.shard.n0 != 0 or self.shard.n1 != N:
-            raise ValueError("GatherGemm shards by M rows only")
+        self.shard = sh = shards[self.rank]
+        if sh.n0 == 0 and sh.n1 == N:        # M-row slabs
+            self.rows, self.cols, self.row_offset, self.col_offset = sh.rows, N, sh.m0, 0
+        elif sh.m0 == 0 and sh.m1 == M_total:  # N-column slabs (multiples of 32 columns)
+            self.rows, self.cols, self.row_offset, self.col_offset = M_total, sh.cols, 0, sh.n0
+        else:
+            raise ValueError("GatherGemm needs whole-row or whole-column slabs")
         nblk_n = (N + MX_BLOCK - 1) // MX_BLOCK
         self.off_s = _round_up(M_total * N, 256)
         self.off_f = _round_up(self.off_s + M_total * nblk_n, 256)
@@ -186,7 +190,7 @@ class GatherGemm:
         self.ds_dest = [ptrs[r] + self.off_s for r in order]
         self.flags = [p + self.off_f for p in ptrs]
         self.epoch = 0
-        ws = mpk.gemm_workspace_size(self.shard.rows, N, K) + K * _round_up(N, 8) * 2 + 256
+        ws = mpk.gemm_workspace_size(self.rows, self.cols, K) + K * _round_up(self.cols, 8) * 2 + 256
         self.workspace = torch.empty(ws, dtype=torch.uint8, device=dev)
         self.D = self.buf[: M_total * N].view(M_total, N)
         self.Ds = self.buf[self.off_s: self.off_s + M_total * nblk_n].view(M_total, nblk_n)
@@ -209,10 +213,13 @@ class GatherGemm:
         self.mpk.peer_barrier(self.flags, self.rank, self.world, self.epoch, stream)
 
     def __call__(self, A_data, A_scales, B, C_data=None, C_scales=None, stream=None):
-        sh = self.shard
+        """Operands are this rank's slab: for M slabs its rows of A and C (B whole),
+        for N slabs A whole and its columns of B, C and C's scales, contiguous
+        (slice_inputs(...) and .contiguous() give them)."""
         self.barrier(stream)
-        self.mpk.gemm_fp8_tensorcore_gather(A_data, A_scales, B, C_data, C_scales, sh.rows, self.N, self.K,
-                                            sh.m0, self.M_total, self.d_dest, self.ds_dest, self.workspace,
-                                            stream)
+        self.mpk.gemm_fp8_tensorcore_gather(A_data, A_scales, B, C_data, C_scales, self.rows, self.cols, self.K,
+                                            self.row_offset, self.M_total, self.d_dest, self.ds_dest,
+                                            self.workspace, stream, col_offset=self.col_offset,
+                                            N_total=self.N)
         self.barrier(stream)
         return self.D, self.Ds

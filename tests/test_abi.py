@@ -144,14 +144,19 @@ def test_collective_entry_points_validate_without_a_device(mpk_lib):
     L = mpk_lib.lib()
     one = (ctypes.c_void_p * 1)(1 << 20)
     nine = (ctypes.c_void_p * 9)(*([1 << 20] * 9))
+    g = L.mpk_gemm_mxfp8_bf16_gather
     # no destinations / too many destinations
-    assert L.mpk_gemm_mxfp8_bf16_gather(None, None, None, None, None, 8, 8, 16, 0, 8, one, one, 0,
-                                        None, 0, None) == MPK_ERR_INVALID_VALUE
-    assert L.mpk_gemm_mxfp8_bf16_gather(None, None, None, None, None, 8, 8, 16, 0, 8, nine, nine, 9,
-                                        None, 0, None) == MPK_ERR_INVALID_VALUE
-    # slab rows past the full D
-    assert L.mpk_gemm_mxfp8_bf16_gather(None, None, None, None, None, 8, 8, 16, 4, 8, one, one, 1,
-                                        None, 0, None) == MPK_ERR_INVALID_VALUE
+    assert g(None, None, None, None, None, 8, 8, 16, 0, 0, 8, 8, one, one, 0, None, 0, None) == \
+        MPK_ERR_INVALID_VALUE
+    assert g(None, None, None, None, None, 8, 8, 16, 0, 0, 8, 8, nine, nine, 9, None, 0, None) == \
+        MPK_ERR_INVALID_VALUE
+    # slab rows past the full D; a column slab past it, or not starting on an MX block
+    assert g(None, None, None, None, None, 8, 8, 16, 4, 0, 8, 8, one, one, 1, None, 0, None) == \
+        MPK_ERR_INVALID_VALUE
+    assert g(None, None, None, None, None, 8, 32, 16, 0, 32, 8, 48, one, one, 1, None, 0, None) == \
+        MPK_ERR_INVALID_VALUE
+    assert g(None, None, None, None, None, 8, 32, 16, 0, 16, 8, 64, one, one, 1, None, 0, None) == \
+        MPK_ERR_INVALID_VALUE
     # barrier: epoch 0, rank outside the world, world above 8
     flags = (ctypes.c_void_p * 2)(1 << 20, 1 << 21)
     assert L.mpk_peer_barrier(flags, 0, 2, 0, None) == MPK_ERR_INVALID_VALUE

@@ -40,6 +40,34 @@ def test_every_destination_gets_the_slab_rows(mpk_lib, cuda, M, N, K, row_offset
     assert mpk_lib.device_status() == 0
 
 
+@pytest.mark.parametrize("M,N,K,col_offset,N_total", [(256, 512, 256, 128, 1024), (130, 100, 64, 64, 164),
+                                                      (96, 96, 32, 0, 192)])
+def test_column_slab_lands_at_its_offset(mpk_lib, cuda, M, N, K, col_offset, N_total):
+    """A column slab's D goes to columns [col_offset, col_offset + N) of every
+    destination (rows N_total bytes apart), its scales to the matching blocks."""
+    import torch
+
+    inp = O.make_gemm_inputs(M, N, K, seed=M + N + col_offset)
+    want_d, want_s = run_gemm(mpk_lib, inp)
+    nb, nbt = (N + 31) // 32, (N_total + 31) // 32
+    A, As, B = to_dev(inp["A_data"]), to_dev(inp["A_scales"]), to_dev(inp["B_bf16"])
+    C, Cs = to_dev(inp["C_data"]), to_dev(inp["C_scales"])
+    Ds = [torch.full((M, N_total), 0xEE, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    Ss = [torch.full((M, nbt), 0xEE, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    ws = torch.empty(mpk_lib.gemm_workspace_size(M, N, K) + 2 * K * (N + 8) + 256, dtype=torch.uint8,
+                     device="cuda")
+    mpk_lib.gemm_fp8_tensorcore_gather(A, As, B, C, Cs, M, N, K, 0, M, Ds, Ss, ws, col_offset=col_offset,
+                                       N_total=N_total)
+    torch.cuda.synchronize()
+    c0, b0 = col_offset, col_offset // 32
+    for d, s in zip(Ds, Ss):
+        d, s = to_host(d), to_host(s)
+        assert np.array_equal(d[:, c0:c0 + N], want_d)
+        assert np.array_equal(s[:, b0:b0 + nb], want_s)
+        assert (d[:, :c0] == 0xEE).all() and (d[:, c0 + N:] == 0xEE).all()
+        assert (s[:, :b0] == 0xEE).all() and (s[:, b0 + nb:] == 0xEE).all()
+
+
 def test_gather_argument_checks(mpk_lib, cuda):
     import torch
 

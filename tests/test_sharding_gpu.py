@@ -57,18 +57,16 @@ def _worker(rank, world, port, q):
             torch.cuda.synchronize()
             ok = bool(torch.equal(D, full_d)) and bool(torch.equal(Ds, full_s))
             q.put((rank, (M, N, K, mode), ok, mpk.device_status()))
-            if m == "m":
-                # the same slabs through the fused GEMM + all-gather, twice (epochs)
-                gg = S.GatherGemm(M, N, K, shards, None)
-                sh = shards[rank]
-                for _ in range(2):
-                    Dg, Dsg = gg(A[sh.m0:sh.m1].contiguous(), As[sh.m0:sh.m1].contiguous(), B,
-                                 C[sh.m0:sh.m1].contiguous(), Cs[sh.m0:sh.m1].contiguous())
-                    torch.cuda.synchronize()
-                    okg = bool(torch.equal(Dg, full_d)) and bool(torch.equal(Dsg, full_s))
-                    q.put((rank, (M, N, K, "fused-gather"), okg, mpk.device_status()))
-                gg.close()
-                del gg
+            # the same slabs through the fused GEMM + all-gather, twice (epochs)
+            gg = S.GatherGemm(M, N, K, shards, None)
+            a, a_s, b, c, c_s = (x.contiguous() for x in S.slice_inputs(shards[rank], m, A, As, B, C, Cs))
+            for _ in range(2):
+                Dg, Dsg = gg(a, a_s, b, c, c_s)
+                torch.cuda.synchronize()
+                okg = bool(torch.equal(Dg, full_d)) and bool(torch.equal(Dsg, full_s))
+                q.put((rank, (M, N, K, "fused-gather-" + m), okg, mpk.device_status()))
+            gg.close()
+            del gg
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -94,8 +92,7 @@ def test_nccl_two_ranks_sharded_gemm(mpk_lib, cuda):
         p.kill()
     assert not alive, "a rank did not finish"
     assert all(p.exitcode == 0 for p in procs)
-    n_m = sum(1 for c in CASES if c[3] == "m")
-    results = [q.get(timeout=10) for _ in range(world * (len(CASES) + 2 * n_m))]
+    results = [q.get(timeout=10) for _ in range(world * 3 * len(CASES))]
     for rank, case, ok, status in results:
         assert ok, (rank, case)
         assert status == 0, (rank, case)
