@@ -10,6 +10,9 @@ if ROOT not in sys.path:
 
 
 def pytest_configure(config):
+    # Temporary files of the tests (tmp_path) stay inside the repository tree.
+    if not config.option.basetemp:
+        config.option.basetemp = os.path.join(ROOT, ".pytest_tmp")
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
     config.addinivalue_line("markers", "needs_ref: needs the reference build in oracle/_ref")
     # The oracle is the checker: build it if this tree has not been built yet.
