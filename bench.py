@@ -125,6 +125,13 @@ class NvmlSampler:
                 return
             time.sleep(self.period)
 
+    def energy_mj(self):
+        """The GPU's cumulative energy counter in millijoules (None if unreadable)."""
+        try:
+            return self.nv.nvmlDeviceGetTotalEnergyConsumption(self.h)
+        except Exception:
+            return None
+
     def stop(self, window=None):
         """Statistics over the samples taken inside window = (t0, t1) (monotonic
         seconds), or over all samples if none fall inside it."""
@@ -159,10 +166,17 @@ class ClockSampler:
     def begin(self):
         """Marks the start of the timed region (host time, just before its launches)."""
         self.window[0] = time.monotonic()
+        self.energy = [self.nvml.energy_mj() if self.nvml.t is not None else None, None]
 
     def end(self):
         """Marks its end (host time, after the device synchronised)."""
         self.window[1] = time.monotonic()
+        self.energy[1] = self.nvml.energy_mj() if self.nvml.t is not None else None
+
+    def joules(self):
+        """GPU energy over the timed region from NVML's counter, or None."""
+        e = getattr(self, "energy", [None, None])
+        return None if None in e else (e[1] - e[0]) / 1000.0
 
     def start(self):
         try:
@@ -410,6 +424,7 @@ def run_gemm_arm(args, world, rank, local, dist):
     e1.record(stream)
     barrier_sync(dist)
     sampler.end()
+    joules = sampler.joules()
     clocks = sampler.stop()
     ms = e0.elapsed_time(e1)
     assert mpk.device_status() == 0, "device wait expired"
@@ -568,6 +583,13 @@ def run_gemm_arm(args, world, rank, local, dist):
     }
     line["clocks"]["samples"] = clocks["samples"]
     line["clocks"]["in_timed_region"] = clocks.get("in_timed_region")
+    if joules:
+        line["energy"] = {"joules_per_step": round(joules / args.steps, 4),
+                          "avg_power_w": round(joules / (ms / 1e3), 1),
+                          "tflop_per_joule": round(flops / 1e12 / (joules / args.steps), 3),
+                          "source": "NVML total energy counter read at the timed region's ends (this "
+                                    "GPU); the counter updates every few tens of ms, so short regions "
+                                    "are approximate or absent"}
     line["clocks"]["nvml_10ms"] = clocks.get("nvml")
     if gather is not None:
         line["gather"] = gather
