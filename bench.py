@@ -715,10 +715,76 @@ def run_codec_arm(args, world, rank, local, dist):
     }
 
 
+def run_reference_codec_arm(args, world):
+    """The reference's host quantize + dequantize (mxfp8_quantize_host,
+    mxfp8_dequantize_host) of 131072 x 2048 FP32, timed on row slabs, one per host
+    thread, and reported in the codec line's unit (GB/s of algorithmic traffic)."""
+    import numpy as np
+
+    import oracle as O
+
+    M, K = 131072, 2048
+    threads = O.default_threads()
+    kind = "reference" if O.ref_available() else "port"
+    rows = int(os.environ.get("MPK_REF_CODEC_ROWS", "128"))
+    rng = np.random.default_rng(45)
+    f32 = ctypes.POINTER(ctypes.c_float)
+    u8 = ctypes.POINTER(ctypes.c_uint8)
+    x = (rng.standard_normal((threads * rows, K)) * 0.02).astype(np.float32)
+    d = np.empty((threads * rows, K), np.uint8)
+    s_ = np.empty((threads * rows, K // 32), np.uint8)
+    y = np.empty_like(x)
+
+    def step():
+        def work(t):
+            r0 = t * rows
+            if kind == "reference":
+                R = O.ref()
+                R.ref_mxfp8_quantize_host(x[r0:r0 + rows].ctypes.data_as(f32), d[r0:r0 + rows].ctypes.data_as(u8),
+                                          s_[r0:r0 + rows].ctypes.data_as(u8), rows, K)
+                R.ref_mxfp8_dequantize_host(d[r0:r0 + rows].ctypes.data_as(u8), s_[r0:r0 + rows].ctypes.data_as(u8),
+                                            y[r0:r0 + rows].ctypes.data_as(f32), rows, K)
+            else:
+                d[r0:r0 + rows], s_[r0:r0 + rows] = O.quantize(x[r0:r0 + rows], threads=1)
+                y[r0:r0 + rows] = O.dequantize(d[r0:r0 + rows], s_[r0:r0 + rows], threads=1)
+
+        ths = [threading.Thread(target=work, args=(t,)) for t in range(threads)]
+        t0 = time.perf_counter()
+        for th in ths:
+            th.start()
+        for th in ths:
+            th.join()
+        return time.perf_counter() - t0
+
+    vals = []
+    sample_bytes = 2 * threads * rows * K * (4 + 1 + 1 / 32)
+    for i in range(args.warmup + args.steps):
+        t = step()
+        if i >= args.warmup:
+            vals.append(sample_bytes / t / 1e9)
+    value = statistics.mean(vals)
+    desc = {"value": value, "unit": "GB/s", "cores": threads, "kind": kind, "cpu_model": cpu_model(),
+            "sample": f"{threads * rows} rows x K={K} quantized and dequantized ({threads} threads x "
+                      f"{rows} rows) per step; mxfp8_quantize_host + mxfp8_dequantize_host"}
+    return {
+        "metric": "MXFP8 quantize+dequantize HBM GB/s (131072x2048 FP32)", "value": value, "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 2 * M * K * (4 + 1 + 1 / 32) / (value * 1e9) * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32/u8", "data": "synthetic N(0,0.02^2)",
+        "impl": "reference", "config": {"workload": "codec quantize+dequantize", "M": M, "K": K,
+                                        "parallelism": "host threads, row slabs"},
+        "cpu_baseline": desc,
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+
+
 def run_reference_arm(args, world, rank):
     if rank != 0:
         return None
-    M, N, K, seed = WORKLOADS.get(args.workload, WORKLOADS["dense_projection"])
+    if args.workload == "codec":
+        return run_reference_codec_arm(args, world)
+    M, N, K, seed = WORKLOADS[args.workload]
     # Each step is a bounded row sample; the per-step budget shrinks with the step
     # count so that the whole run stays within about two minutes of host work.
     budget = float(os.environ.get("MPK_REF_STEP_BUDGET_S", "2.0"))
@@ -777,11 +843,15 @@ def main():
             line = run_codec_arm(args, world, rank, local, dist)
         else:
             line = run_gemm_arm(args, world, rank, local, dist)
-        if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload != "codec":
-            M, N, K, seed = WORKLOADS[args.workload]
-            _, desc = cpu_baseline(M, N, K, seed, args.cpu_budget_s)
-            desc["cpu_model"] = cpu_model()
-            line["cpu_baseline"] = desc
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            if args.workload == "codec":
+                sub = argparse.Namespace(steps=3, warmup=1)
+                line["cpu_baseline"] = run_reference_codec_arm(sub, 1)["cpu_baseline"]
+            else:
+                M, N, K, seed = WORKLOADS[args.workload]
+                _, desc = cpu_baseline(M, N, K, seed, args.cpu_budget_s)
+                desc["cpu_model"] = cpu_model()
+                line["cpu_baseline"] = desc
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:
