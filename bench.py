@@ -694,6 +694,32 @@ def run_codec_arm(args, world, rank, local, dist):
     qg, dg = bytes_one / q_ms / 1e6, bytes_one / dq_ms / 1e6
     q_ms_max, dq_ms_max = max_over_ranks(dist, q_ms), max_over_ranks(dist, dq_ms)
     value = world * bytes_one * 2 / ((q_ms_max + dq_ms_max) / 1e3) / 1e9
+
+    # End to end: every step uploads the FP32 tensor from pinned host memory,
+    # quantizes and dequantizes it through the C ABI, and downloads the result.
+    del x16
+    hx = torch.empty((M, K), dtype=torch.float32).pin_memory()
+    hx.copy_(x)
+    y = torch.empty_like(x)
+    hy = torch.empty_like(hx).pin_memory()
+
+    def e2e_step():
+        x.copy_(hx, non_blocking=True)
+        L.mpk_mxfp8_quantize(x.data_ptr(), d.data_ptr(), s.data_ptr(), M, K, sptr)
+        L.mpk_mxfp8_dequantize(d.data_ptr(), s.data_ptr(), y.data_ptr(), M, K, sptr)
+        hy.copy_(y, non_blocking=True)
+
+    e2e_steps = 3
+    e2e_step()
+    barrier_sync(dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier_sync(dist)
+    e2e_ms = max_over_ranks(dist, e0.elapsed_time(e1) / e2e_steps)
+    e2e_value = world * bytes_one * 2 / (e2e_ms / 1e3) / 1e9
     return {
         "metric": "MXFP8 quantize+dequantize HBM GB/s (131072x2048 FP32)", "value": round(value, 1),
         "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -702,6 +728,9 @@ def run_codec_arm(args, world, rank, local, dist):
         "config": {"workload": "codec quantize+dequantize", "M": M, "K": K,
                    "l2": "1 GiB FP32 tensor > L2"},
         "gpu_launches": 2 * args.steps,
+        "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": M * K * 4,
+                "d2h_bytes_per_step": M * K * 4, "steps": e2e_steps,
+                "what": "pinned FP32 upload, quantize, dequantize, pinned FP32 download, every step"},
         "bf16_companions": {"quantize_bf16_gbs": round(bytes16 / qb_ms / 1e6, 1),
                             "quantize_bf16_frac": round(bytes16 / qb_ms / 1e6 / hbm, 4),
                             "dequantize_bf16_gbs": round(bytes16 / db_ms / 1e6, 1),
