@@ -1,28 +1,37 @@
 // D = A*B + C with A in MXFP8, B in BF16 and C/D in MXFP8 (blocks along N):
-// a persistent, warp-specialised, 2-CTA tcgen05 kernel for sm_100a.
+// persistent, warp-specialised, 2-CTA tcgen05 kernels for sm_100a.
 //
 // Replaces the reference's launcher gemm_fp8_tensorcore
 // (src/kernels/gemm_fp8_tensorcore.cu:231-249), which runs a WMMA fp16 kernel
 // into an FP32 temporary it allocates per call, then quantizes that temporary in
-// a second kernel.  Here the whole path is one kernel and allocates nothing.
+// a second kernel.  Here the +C and the MXFP8 quantization of D are fused into the
+// GEMM's epilogue.
+//
+// Two kernels share the work decomposition, the pair MMA and the epilogue:
+//   gemm_bf16a_mxfp8_kernel  (the default path) A was dequantized exactly to BF16
+//                            by a bandwidth pre-pass (codec.cu); both operands
+//                            arrive by TMA.  Optionally forwards D tiles to other
+//                            GPUs (the fused all-gather).
+//   gemm_mxfp8_bf16_kernel   (the allocation-free variant) A arrives as E4M3 codes
+//                            and transform warps convert it to BF16 in shared memory.
 //
 // Work decomposition.  Clusters of two CTAs on neighbouring SMs own 256 x 256
-// output tiles (persistent, tiles strided by the number of clusters, M fastest).
-// CTA rank r of the pair owns output rows [m0 + 128 r, +128) and loads only its
-// half of the tile's B columns, [n0 + 128 r, +128): the pair MMA
+// output tiles (persistent, work items strided by the number of clusters, in the
+// panel raster of tile_coords; the last partial wave may be cut into 256 x 128
+// items, item_coords).  CTA rank r of the pair owns output rows [m0 + 128 r, +128)
+// and loads only its half of the tile's B columns, [n0 + 128 r, +128): the pair MMA
 // (tcgen05.mma.cta_group::2, M=256 N=256 K=16, issued by rank 0) reads A rows from
 // each CTA's own shared memory and B columns from both, and writes each CTA's
 // 128 x 256 FP32 accumulator into that CTA's tensor memory.  Versus one CTA per
 // 128 x 256 tile this halves the B bytes each SM pulls from L2 per MMA.
 //
-// Per CTA and per K-step of 64 (STAGES-deep ring):
+// On-chip variant, per CTA and per K-step of 64 (STAGES-deep ring):
 //   A codes  u8   128 x 64   8 KiB  TMA (64-byte swizzle), completes on this CTA's full_a8
 //   A bf16        128 x 64  16 KiB  written by the transform warps, K-major, 128-byte
 //                                   swizzle (the UMMA canonical layout)
 //   B bf16         64 x 128 16 KiB  TMA, two 64x64 boxes, 128-byte swizzle, MN-major;
 //                                   completes on rank 0's full_b (.cta_group::2)
-//
-// Warp roles (per CTA):
+// Warp roles of the on-chip variant (per CTA):
 //   warp 0   TMA producer (one lane)
 //   warp 1   TMEM owner (cta_group::2 allocation); on rank 0 also the MMA issuer
 //   warps 2+ transform: E4M3 code x 2^(scale-127) -> BF16 in shared memory (exact for
@@ -30,6 +39,7 @@
 //            full_a16 barrier
 //   last 4   epilogue: tcgen05.ld of this CTA's accumulator rows, + dequantized C,
 //            per-32-column amax, E8M0 scale, RNE E4M3, 16-byte stores
+// (The BF16-A kernel's ring and roles are described at its definition.)
 //
 // Every mbarrier wait is bounded (mpk::mbar_wait*); on expiry the CTA raises an
 // abort flag, records a status code, drains the copies and MMAs it has in
