@@ -871,7 +871,9 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
 // BF16 A rows (16 KiB, 128-byte swizzle = the UMMA K-major layout) and its 64 x 128
 // B half (16 KiB), both completing on rank 0's full barrier.
 //
-// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer (rank 0), 2-3 idle, 4-7 epilogue.
+// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer (rank 0), 2-3 copy warps of the
+// fused all-gather (idle otherwise), 4-7 epilogue.  Launched after the A pre-pass with
+// programmatic stream serialization: only the producer waits for the pre-pass.
 // ============================================================================
 #ifndef MPK_P_STAGES
 #define MPK_P_STAGES 7
