@@ -1,7 +1,7 @@
 """Benchmark of the MXFP8 x BF16 GEMM path (D = A*B + C) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload dense_projection|long_k|tall_skinny|wide|square|codec] [--gather]
+                    [--workload dense_projection|long_k|tall_skinny|wide|square|codec] [--no-gather]
 
 One step is one pass of the hot path over one batch of synthetic input: one
 D = A*B + C call at the workload's shape (default: the dense projection
@@ -531,7 +531,7 @@ def run_gemm_arm(args, world, rank, local, dist):
     # cap acting during the timed region, in which case the sustained figure (the
     # same GEMM measured back to back under the cap).  Both fractions are reported.
     gather = gather_measurement(args, world, rank, dist, mpk, L, M, N, K, Ad, As, B, Cd, Cs, D, Ds, stream) \
-        if world > 1 and args.gather else None
+        if world > 1 and not args.no_gather else None
 
     peaks, peak_src = load_peaks()
     burst = float(peaks["bf16_tflops"])
@@ -852,9 +852,9 @@ def main():
     ap.add_argument("--cpu-budget-s", type=float, default=12.0,
                     help="seconds of host work for the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--gather", action="store_true",
-                    help="with --gpus > 1: also time the fused GEMM + all-gather of D against the GEMM "
-                         "followed by NCCL all_gather_into_tensor")
+    ap.add_argument("--no-gather", action="store_true",
+                    help="with --gpus > 1: skip timing the fused GEMM + all-gather of D against the GEMM "
+                         "followed by NCCL all_gather_into_tensor (reported as `gather`)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
