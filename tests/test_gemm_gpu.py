@@ -153,6 +153,32 @@ def test_a_exotic_scales_and_nan_codes(mpk_lib, cuda, with_nan):
     assert hist[0] + hist[1] >= WITHIN_ONE_STEP * sum(hist)
 
 
+def test_special_values_in_b_and_c(mpk_lib, cuda):
+    """NaN and +-inf in B and NaN codes in C propagate as in the FP32 gold (the
+    reference's order of operations), and blocks holding them quantize by the
+    reference's rule: amax ignores NaN, an infinite amax gives scale byte 255 and
+    NaN codes."""
+    M, N, K = 128, 256, 128
+    inp = O.make_gemm_inputs(M, N, K, seed=123)
+    rng = np.random.default_rng(123)
+    b = inp["B_bf16"].copy()
+    idx = rng.choice(K * N, 12, replace=False)
+    b.ravel()[idx] = rng.choice(np.array([0x7FC0, 0x7F80, 0xFF80], np.uint16), 12)  # NaN, +inf, -inf
+    inp["B_bf16"] = b
+    inp["B_f32"] = O.bf16_bits_to_float(b)
+    c = inp["C_data"].copy()
+    c.ravel()[rng.choice(M * N, 10, replace=False)] = 0x7F
+    inp["C_data"] = c
+    inp["C_deq"] = O.dequantize(c, inp["C_scales"])
+    Dd, Ds = run_gemm(mpk_lib, inp)
+    gold = O.gold_mx(inp)
+    hist = O.mx_ulp_hist(Dd, Ds, gold[1], gold[2])
+    print(f"special values in B and C: {hist}")
+    assert hist[3] == 0
+    assert hist[0] + hist[1] >= WITHIN_ONE_STEP * sum(hist)
+    assert (Ds == 255).any() and (Dd == 0x7F).any()
+
+
 def test_k_zero_is_requantized_c(mpk_lib, cuda):
     import torch
 
