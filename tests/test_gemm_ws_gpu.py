@@ -159,3 +159,43 @@ def test_split_tail_with_empty_half(mpk_lib, cuda):
     Dd, Ds = run_gemm(mpk_lib, inp)
     check_parity(Dd, Ds, O.gold_mx(inp), f"split tail {M}x{N}x{K}")
     assert mpk_lib.device_status() == 0
+
+
+def test_concurrent_streams_and_threads(mpk_lib, cuda):
+    """Calls in flight on several streams at once, issued from several host
+    threads, each with its own pooled workspace: every D equals the same call made
+    alone."""
+    import threading
+
+    import torch
+
+    shapes = [(512, 768, 256), (1024, 512, 384), (256, 2048, 128), (768, 1024, 512)]
+    cases = []
+    for i, (M, N, K) in enumerate(shapes):
+        inp = O.make_gemm_inputs(M, N, K, seed=300 + i)
+        want = run_gemm(mpk_lib, inp)
+        dev = [to_dev(inp[k]) for k in ("A_data", "A_scales", "B_bf16", "C_data", "C_scales")]
+        D = torch.empty((M, N), dtype=torch.uint8, device="cuda")
+        Ds = torch.empty((M, N // 32), dtype=torch.uint8, device="cuda")
+        cases.append(((M, N, K), dev, D, Ds, want, torch.cuda.Stream()))
+    torch.cuda.synchronize()
+    errors = []
+
+    def worker(case):
+        (M, N, K), (A, As, B, C, Cs), D, Ds, _, st = case
+        try:
+            for _ in range(5):
+                mpk_lib.gemm_fp8_tensorcore(A, As, B, C, Cs, D, Ds, M, N, K, st)
+        except Exception as e:  # reported below
+            errors.append(e)
+
+    ths = [threading.Thread(target=worker, args=(c,)) for c in cases]
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    torch.cuda.synchronize()
+    assert not errors, errors
+    for _, _, D, Ds, (wd, ws_), _ in cases:
+        assert np.array_equal(to_host(D), wd) and np.array_equal(to_host(Ds), ws_)
+    assert mpk_lib.device_status() == 0
