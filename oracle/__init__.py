@@ -1,7 +1,7 @@
 """CPU oracle for the MXFP8 x BF16 GEMM path.  TEST INFRASTRUCTURE ONLY.
 
 Only the test suite, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
-``bench.py`` import this package; it is the checker, never the thing measured or
+``bench.py`` import this package; it checks results and is never the thing measured or
 shipped.  The product library (``mix_precision_kernel_b200``) has no CPU path.
 
 Two shared libraries back it:

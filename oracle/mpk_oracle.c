@@ -1,7 +1,7 @@
 /*
  * CPU oracle for the MXFP8 x BF16 GEMM path (D = A*B + C) and the MXFP8 codec.
  *
- * TEST INFRASTRUCTURE ONLY.  This file is the checker, not the product: only the
+ * TEST INFRASTRUCTURE ONLY.  This file checks results and is not the product: only the
  * test suite, the smoke check and the benchmark's CPU-baseline leg load it.  The
  * CUDA library never calls into it and has no CPU fallback.
  *

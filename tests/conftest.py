@@ -15,7 +15,7 @@ def pytest_configure(config):
         config.option.basetemp = os.path.join(ROOT, ".pytest_tmp")
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
     config.addinivalue_line("markers", "needs_ref: needs the reference build in oracle/_ref")
-    # The oracle is the checker: build it if this tree has not been built yet.
+    # The parity tests need the oracle: build it if this tree has not been built yet.
     oracle_so = os.path.join(ROOT, "oracle", "_build", "libmpk_oracle.so")
     if not os.path.exists(oracle_so):
         subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "oracle"], check=True)
