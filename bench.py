@@ -583,13 +583,14 @@ def run_gemm_arm(args, world, rank, local, dist):
     }
     line["clocks"]["samples"] = clocks["samples"]
     line["clocks"]["in_timed_region"] = clocks.get("in_timed_region")
-    if joules:
+    # The counter moves in steps of tens of milliseconds: shorter regions gave
+    # average powers above the board limit, so energy is reported from 1 s up.
+    if joules and ms >= 1000.0:
         line["energy"] = {"joules_per_step": round(joules / args.steps, 4),
                           "avg_power_w": round(joules / (ms / 1e3), 1),
                           "tflop_per_joule": round(flops / 1e12 / (joules / args.steps), 3),
                           "source": "NVML total energy counter read at the timed region's ends (this "
-                                    "GPU); the counter updates every few tens of ms, so short regions "
-                                    "are approximate or absent"}
+                                    "GPU); reported for timed regions of 1 s or more"}
     line["clocks"]["nvml_10ms"] = clocks.get("nvml")
     if gather is not None:
         line["gather"] = gather
