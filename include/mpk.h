@@ -77,8 +77,41 @@ int mpk_gemm_mxfp8_bf16_ws(const uint8_t* A_data, const uint8_t* A_scales, const
 
 /* Workspace bytes mpk_gemm_mxfp8_bf16_ws needs for an M x N x K product with a
  * 16-byte aligned B: M * roundup(K, 8) * 2, rounded up to 256, plus
- * K * roundup(N, 8) * 2 when N % 8 != 0. */
+ * K * roundup(N, 8) * 2 when N % 8 != 0, plus, when the current schedule spreads the
+ * last partial wave of tiles over the SMs (stream-K, see mpk_gemm_plan), 256 KiB per
+ * participating SM pair and a few hundred bytes of counters (at most 18.5 MiB +
+ * 1 KiB on a 148-SM B200).  A workspace with room for the operands but not for the
+ * stream-K partials is accepted; the kernel then runs whole tiles only.  The size
+ * depends on the current device's SM count and on mpk_set_gemm_schedule. */
 int mpk_gemm_workspace_size(int M, int N, int K, size_t* bytes);
+
+/* Work schedule of the tensor-core kernel of mpk_gemm_mxfp8_bf16 and its _ws and
+ * _noalloc forms (process-wide; the fused all-gather always runs whole tiles).
+ *   MPK_SCHEDULE_AUTO      (default) whole 256x256 tiles in waves over the SM pairs;
+ *                          the tiles of a last, partial wave are spread over all
+ *                          pairs by K-step ranges (stream-K): each pair computes a
+ *                          contiguous range of K-steps, a tile split across pairs is
+ *                          finished by the pair holding its last K-steps after adding
+ *                          the others' FP32 partial sums.  Used when it keeps more
+ *                          pairs busy than whole tiles would and gives each pair at
+ *                          least 8 K-steps of 64; otherwise a partial wave of at most
+ *                          half the pairs is cut into 256x128 tiles.
+ *   MPK_SCHEDULE_TILES     whole tiles only (the split last wave as above).  D is
+ *                          then the same for any schedule of the same tiles (every
+ *                          element summed in one K order).
+ *   MPK_SCHEDULE_STREAM_K  every tile's K-steps spread over the SM pairs (testing).
+ * Split tiles sum their K ranges in a different order than whole tiles, so D may
+ * differ between schedules by one E4M3 step in rare elements; for a given shape,
+ * device and schedule it is deterministic.  No counterpart in the reference. */
+enum { MPK_SCHEDULE_AUTO = 0, MPK_SCHEDULE_TILES = 1, MPK_SCHEDULE_STREAM_K = 2 };
+int mpk_set_gemm_schedule(int schedule);
+int mpk_gemm_schedule(void);
+
+/* The schedule an M x N x K product gets on the current device: *stream_k_tiles
+ * tiles (the first of the tile raster) spread over *stream_k_pairs SM pairs, the rest
+ * whole tiles; *tiles is the total number of 256x256 tiles.  No counterpart in the
+ * reference. */
+int mpk_gemm_plan(int M, int N, int K, int* tiles, int* stream_k_tiles, int* stream_k_pairs);
 
 /* Returns the current device's pooled GEMM workspace to the driver, once the
  * work queued on it has finished.  No counterpart in the reference. */
@@ -93,15 +126,21 @@ int mpk_release_workspace_pool(void);
 /* Same computation as mpk_gemm_mxfp8_bf16, for callers that may not allocate
  * device memory once running (a caching allocator that has reserved the device, a
  * latency-bound loop, a fixed memory budget).  The A workspace is a fixed array in
- * the library's device image (MPK_NOALLOC_SCRATCH_BYTES per device, held from
- * the image's load); this call allocates nothing.  Sizes whose workspace exceeds
- * that return MPK_ERR_UNSUPPORTED.  Nothing in the array needs to start at zero.
- * All calls on a device share the array: calls that can run at the same time
- * (different streams without an event between them, or unordered host threads)
- * race, so issue them on one stream or order them.  The first call on each device
- * looks up the array's address; if that first call would be made inside a stream
- * capture, make one call before the capture instead.  No counterpart in the
- * reference. */
+ * the library's device image (MPK_NOALLOC_SCRATCH_BYTES per device, held until the
+ * process exits); after the first call on a device, calls allocate nothing.  With
+ * CUDA's default lazy module loading the array is reserved by that first call on
+ * each device (when it loads the image holding the array), so make one call during
+ * set-up, before a caching allocator reserves the device's memory and before any
+ * stream capture (or run with CUDA_MODULE_LOADING=EAGER, which reserves it when the
+ * context is created).  The array's address is looked up on every call, so calls
+ * stay valid after cudaDeviceReset (whose next first call reserves it again).
+ * Sizes whose workspace exceeds the array return MPK_ERR_UNSUPPORTED.  Nothing in
+ * the array needs to start at zero.  When the array also has room for the
+ * stream-K partials (see mpk_set_gemm_schedule) the call uses them, otherwise it
+ * runs whole tiles.  All calls on a device share the array: calls that can run at
+ * the same time (different streams without an event between them, or unordered
+ * host threads) race, so issue them on one stream or order them.  No counterpart
+ * in the reference. */
 int mpk_gemm_mxfp8_bf16_noalloc(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
                                 const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                                 uint8_t* D_scales, int M, int N, int K, void* stream);
@@ -194,8 +233,10 @@ int mpk_set_wait_timeout_ns(uint64_t ns);
 int mpk_wait_selftest(uint64_t timeout_ns, void* stream);
 
 /* Static description of a status code, and the detail of the last failure on
- * the calling thread. */
+ * the calling thread (mpk_last_error_string; mpk_last_error is the same function
+ * under its earlier name). */
 const char* mpk_status_string(int status);
+const char* mpk_last_error_string(void);
 const char* mpk_last_error(void);
 
 /* Library version (major*10000 + minor*100 + patch). */

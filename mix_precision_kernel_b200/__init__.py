@@ -31,6 +31,7 @@ __all__ = [
     "ipc_export", "ipc_import", "ipc_close",
     "gemm_fp8_tensorcore_noalloc", "NOALLOC_SCRATCH_BYTES",
     "gemm", "quantize", "dequantize", "device_status", "set_wait_timeout_ns", "wait_selftest",
+    "set_gemm_schedule", "gemm_schedule", "gemm_plan", "SCHEDULE_AUTO", "SCHEDULE_TILES", "SCHEDULE_STREAM_K",
     "MX_BLOCK", "nblk",
 ]
 
@@ -47,6 +48,11 @@ MPK_ERR_MISALIGNED = 1003
 MPK_ERR_DEVICE_TIMEOUT = 1004
 MPK_ERR_ARCH = 1005
 MPK_ERR_DRIVER = 1006
+
+# GEMM work schedules (MPK_SCHEDULE_* in include/mpk.h)
+SCHEDULE_AUTO = 0
+SCHEDULE_TILES = 1
+SCHEDULE_STREAM_K = 2
 
 
 class MpkError(RuntimeError):
@@ -99,13 +105,20 @@ def lib() -> ctypes.CDLL:
             L.mpk_status_string.restype = ctypes.c_char_p
             L.mpk_last_error.argtypes = []
             L.mpk_last_error.restype = ctypes.c_char_p
+            L.mpk_last_error_string.argtypes = []
+            L.mpk_last_error_string.restype = ctypes.c_char_p
+            L.mpk_set_gemm_schedule.argtypes = [ci]
+            L.mpk_gemm_schedule.argtypes = []
+            ip = ctypes.POINTER(ci)
+            L.mpk_gemm_plan.argtypes = [ci, ci, ci, ip, ip, ip]
             for f in ("mpk_gemm_mxfp8_bf16", "mpk_gemm_mxfp8_bf16_ws", "mpk_gemm_workspace_size",
                       "mpk_release_workspace_pool", "mpk_mxfp8_quantize", "mpk_mxfp8_dequantize",
                       "mpk_mxfp8_dequantize_bf16", "mpk_gemm_mxfp8_bf16_noalloc",
                       "mpk_mxfp8_quantize_bf16", "mpk_gemm_mxfp8_bf16_gather", "mpk_peer_barrier",
                       "mpk_ipc_export", "mpk_ipc_import", "mpk_ipc_close",
                       "mpk_mxfp8_quantize_host", "mpk_mxfp8_dequantize_host", "mpk_device_status",
-                      "mpk_set_wait_timeout_ns", "mpk_wait_selftest", "mpk_version"):
+                      "mpk_set_wait_timeout_ns", "mpk_wait_selftest", "mpk_version",
+                      "mpk_set_gemm_schedule", "mpk_gemm_schedule", "mpk_gemm_plan"):
                 getattr(L, f).restype = ci
             _lib = L
     return _lib
@@ -114,7 +127,7 @@ def lib() -> ctypes.CDLL:
 def _check(status: int) -> None:
     if status != MPK_SUCCESS:
         L = lib()
-        detail = (L.mpk_last_error() or b"").decode(errors="replace")
+        detail = (L.mpk_last_error_string() or b"").decode(errors="replace")
         msg = L.mpk_status_string(status).decode(errors="replace")
         raise MpkError(status, f"{msg}; {detail}" if detail else msg)
 
@@ -298,6 +311,27 @@ def set_wait_timeout_ns(ns: int) -> None:
 
 def wait_selftest(timeout_ns: int, stream=None) -> None:
     _check(lib().mpk_wait_selftest(int(timeout_ns), _stream(stream)))
+
+
+def set_gemm_schedule(schedule: int) -> int:
+    """Sets the process-wide GEMM work schedule (SCHEDULE_AUTO, SCHEDULE_TILES or
+    SCHEDULE_STREAM_K); returns the previous one."""
+    L = lib()
+    prev = L.mpk_gemm_schedule()
+    _check(L.mpk_set_gemm_schedule(int(schedule)))
+    return prev
+
+
+def gemm_schedule() -> int:
+    return lib().mpk_gemm_schedule()
+
+
+def gemm_plan(M: int, N: int, K: int) -> tuple[int, int, int]:
+    """(tiles, stream-K tiles, stream-K SM pairs) of an M x N x K product on the
+    current device under the current schedule."""
+    t, st, sp = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    _check(lib().mpk_gemm_plan(M, N, K, ctypes.byref(t), ctypes.byref(st), ctypes.byref(sp)))
+    return t.value, st.value, sp.value
 
 
 # ---------------------------------------------------------------------------

@@ -124,7 +124,24 @@ extern "C" {
 
 int mpk_version(void) { return 100; }
 
+const char* mpk_last_error_string(void) { return t_last_error; }
 const char* mpk_last_error(void) { return t_last_error; }
+
+int mpk_set_gemm_schedule(int schedule) { return gemm_set_schedule(schedule); }
+int mpk_gemm_schedule(void) { return gemm_schedule(); }
+
+int mpk_gemm_plan(int M, int N, int K, int* tiles, int* stream_k_tiles, int* stream_k_pairs)
+{
+    if (!tiles || !stream_k_tiles || !stream_k_pairs || M < 0 || N < 0 || K < 0) {
+        set_last_error("mpk_gemm_plan: null output or negative size");
+        return MPK_ERR_INVALID_VALUE;
+    }
+    const SkPlan plan = gemm_sk_plan(M, N, K);
+    *tiles = (int)((((int64_t)M + 255) / 256) * (((int64_t)N + 255) / 256));
+    *stream_k_tiles = plan.tiles;
+    *stream_k_pairs = plan.clusters;
+    return MPK_SUCCESS;
+}
 
 const char* mpk_status_string(int status)
 {
@@ -208,6 +225,18 @@ static cudaMemPool_t workspace_pool(bool create)
     return g_pools[dev];
 }
 
+// Drops the current device's pool handle (after its context was destroyed).
+static void forget_workspace_pool()
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return;
+    }
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    g_pools[dev] = nullptr;
+}
+
 int mpk_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
                         const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                         uint8_t* D_scales, int M, int N, int K, void* stream)
@@ -238,12 +267,19 @@ int mpk_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const vo
     cudaError_t ae = cudaErrorNotReady;
     if (cs == cudaStreamCaptureStatusNone) {
         if (cudaMemPool_t pool = workspace_pool(true)) ae = cudaMallocFromPoolAsync(&ws, need, pool, st);
+        if (ae == cudaErrorInvalidValue) {
+            // The pool belonged to a context that cudaDeviceReset destroyed: make a
+            // new one and try once more.
+            cudaGetLastError();
+            forget_workspace_pool();
+            if (cudaMemPool_t pool = workspace_pool(true)) ae = cudaMallocFromPoolAsync(&ws, need, pool, st);
+        }
     } else if (cs == cudaStreamCaptureStatusActive) {
         ae = cudaMallocAsync(&ws, need, st);
     }
     if (ae == cudaSuccess) {
         const int rc = launch_gemm_mxfp8_bf16_prepass(A_data, A_scales, B_bf16, C_data, C_scales, D_data,
-                                                      D_scales, M, N, K, ws, st);
+                                                      D_scales, M, N, K, ws, need, st);
         const cudaError_t fe = cudaFreeAsync(ws, st);
         return rc ? rc : from_cuda(fe, "workspace release");
     }
@@ -286,7 +322,7 @@ int mpk_gemm_mxfp8_bf16_ws(const uint8_t* A_data, const uint8_t* A_scales, const
                                       N, K, (cudaStream_t)stream);
     }
     const bool copy_b = gemm_b_needs_copy(B_bf16, N);
-    const size_t need = gemm_workspace_bytes(M, N, K, copy_b);
+    const size_t need = gemm_workspace_bytes_min(M, N, K, copy_b);
     if (workspace_bytes < need) {
         set_last_error("workspace of %zu bytes needed%s, got %zu", need,
                        copy_b && N % 8 == 0 ? " (B is not 16-byte aligned, so a padded copy of B is "
@@ -299,7 +335,7 @@ int mpk_gemm_mxfp8_bf16_ws(const uint8_t* A_data, const uint8_t* A_scales, const
         return MPK_ERR_MISALIGNED;
     }
     return launch_gemm_mxfp8_bf16_prepass(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales,
-                                          M, N, K, workspace, (cudaStream_t)stream);
+                                          M, N, K, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 int mpk_gemm_mxfp8_bf16_gather(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
@@ -362,7 +398,7 @@ int mpk_gemm_mxfp8_bf16_gather(const uint8_t* A_data, const uint8_t* A_scales, c
         }
         return MPK_SUCCESS;
     }
-    const size_t need = gemm_workspace_bytes(M, N, K, gemm_b_needs_copy(B_bf16, N));
+    const size_t need = gemm_workspace_bytes_min(M, N, K, gemm_b_needs_copy(B_bf16, N));
     if (!workspace || workspace_bytes < need) {
         set_last_error("fused all-gather needs a workspace of %zu bytes, got %zu", need, workspace_bytes);
         return MPK_ERR_INVALID_VALUE;
@@ -382,7 +418,7 @@ int mpk_gemm_mxfp8_bf16_gather(const uint8_t* A_data, const uint8_t* A_scales, c
         g.Ds_extra[d - 1] = Ds_dest[d];
     }
     return launch_gemm_mxfp8_bf16_prepass(A_data, A_scales, B_bf16, C_data, C_scales, D_dest[0], Ds_dest[0],
-                                          M, N, K, workspace, st, &g);
+                                          M, N, K, workspace, workspace_bytes, st, &g);
 }
 
 int mpk_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t epoch, void* stream)
@@ -545,7 +581,14 @@ int mpk_wait_selftest(uint64_t timeout_ns, void* stream)
 // mpk_gemm_mxfp8_bf16 (A pre-pass, then the tensor-core kernel) with the BF16 copy
 // of A in the fixed array below, which is part of the library's device image: it
 // takes MPK_NOALLOC_SCRATCH_BYTES of device memory on each device from the moment
-// the image is loaded there, and the call path itself allocates nothing.
+// the image is loaded there, and the call path itself allocates nothing.  With
+// CUDA's default lazy loading, the image that holds the array (this file's device
+// code, which has no kernels) is loaded on a device by the first
+// mpk_gemm_mxfp8_bf16_noalloc call there, when that call looks up the array's
+// address: that first call is when the device memory is taken, so callers that
+// reserve the device's memory for a caching allocator make one call before they do
+// (or set CUDA_MODULE_LOADING=EAGER, which loads it when the CUDA context is
+// created).
 //
 // Contents: nothing in the array has to start at zero or hold anything between
 // calls.  Each call's pre-pass writes all M*K*2 bytes that the call's GEMM kernel
@@ -559,30 +602,19 @@ int mpk_wait_selftest(uint64_t timeout_ns, void* stream)
 // stream, or order them with events.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[MPK_NOALLOC_SCRATCH_BYTES];
 
-namespace {
-std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64] = {};
-}  // namespace
-
-// Device address of g_noalloc_scratch on the current device, looked up once per
-// device (with that device current) and cached.
+// Device address of g_noalloc_scratch in the current device's context.  In host
+// code the array's name is only a stand-in, so the address is asked of the runtime,
+// with the device current, on every call: it is valid only for the context that
+// loaded this device code, and is not kept across calls, so a context re-created
+// after cudaDeviceReset gets its own array's address.  Once the code is loaded the
+// lookup is a table search; the first lookup on a device (or on a re-created
+// context) loads it, which is when the array is reserved.
 static int noalloc_scratch(void** out)
 {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return from_cuda(e, "cudaGetDevice");
-    if (dev < 0 || dev >= 64) {
-        set_last_error("device ordinal %d out of range", dev);
-        return MPK_ERR_INVALID_VALUE;
-    }
-    std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!g_noalloc_addr[dev]) {
-        void* ptr = nullptr;
-        e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_scratch);
-        if (e != cudaSuccess) return from_cuda(e, "cudaGetSymbolAddress of the no-alloc scratch");
-        g_noalloc_addr[dev] = ptr;
-    }
-    *out = g_noalloc_addr[dev];
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return from_cuda(e, "cudaGetSymbolAddress of the no-alloc scratch");
+    *out = ptr;
     return MPK_SUCCESS;
 }
 
@@ -599,7 +631,7 @@ extern "C" int mpk_gemm_mxfp8_bf16_noalloc(const uint8_t* A_data, const uint8_t*
     if (K == 0)
         return from_cuda(launch_mxfp8_requantize(C_data, C_scales, D_data, D_scales, M, N, st),
                          "requantize launch");
-    const size_t need = gemm_workspace_bytes(M, N, K, gemm_b_needs_copy(B_bf16, N));
+    const size_t need = gemm_workspace_bytes_min(M, N, K, gemm_b_needs_copy(B_bf16, N));
     if (need > (size_t)MPK_NOALLOC_SCRATCH_BYTES) {
         set_last_error("mpk_gemm_mxfp8_bf16_noalloc: the workspace of %zu bytes exceeds its fixed scratch "
                        "of %zu bytes (M*K <= %zu for K %% 8 == 0, N %% 8 == 0 and 16-byte aligned B); use "
@@ -610,5 +642,5 @@ extern "C" int mpk_gemm_mxfp8_bf16_noalloc(const uint8_t* A_data, const uint8_t*
     void* scratch = nullptr;
     if (int rc = noalloc_scratch(&scratch)) return rc;
     return launch_gemm_mxfp8_bf16_prepass(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales,
-                                          M, N, K, scratch, st);
+                                          M, N, K, scratch, (size_t)MPK_NOALLOC_SCRATCH_BYTES, st);
 }

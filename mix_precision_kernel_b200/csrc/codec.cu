@@ -284,11 +284,20 @@ __device__ __forceinline__ uint4 e4m3x8_to_bf16x8(uint2 c, uint32_t s)
 // the GEMM that reads it next.
 constexpr int kPrepassU = 2;
 
+// Block 0 of the A pre-pass zeroes the GEMM's stream-K counters (n_zero words).
+__device__ __forceinline__ void zero_words_block0(uint32_t* words, int n)
+{
+    if (blockIdx.x == 0)
+        for (int i = threadIdx.x; i < n; i += blockDim.x) words[i] = 0u;
+}
+
 __global__ void __launch_bounds__(kCodecThreads)
 mxfp8_dequantize_bf16_flat_kernel(const uint8_t* __restrict__ data, const uint8_t* __restrict__ scales,
-                                  uint16_t* __restrict__ out, int64_t n_octets)
+                                  uint16_t* __restrict__ out, int64_t n_octets, uint32_t* zero_words,
+                                  int n_zero)
 {
     allow_dependent_launch();
+    zero_words_block0(zero_words, n_zero);
     const int lane = threadIdx.x & 31;
     const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -313,9 +322,10 @@ mxfp8_dequantize_bf16_flat_kernel(const uint8_t* __restrict__ data, const uint8_
 __global__ void __launch_bounds__(kCodecThreads)
 mxfp8_dequantize_bf16_elem_kernel(const uint8_t* __restrict__ data, const uint8_t* __restrict__ scales,
                                   uint16_t* __restrict__ out, int64_t M, int64_t K, int64_t nblk,
-                                  int64_t ld_out)
+                                  int64_t ld_out, uint32_t* zero_words, int n_zero)
 {
     allow_dependent_launch();
+    zero_words_block0(zero_words, n_zero);
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M * K; i += stride) {
         const int64_t row = i / K, k = i % K;
@@ -388,7 +398,8 @@ cudaError_t launch_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, 
 }
 
 cudaError_t launch_mxfp8_dequantize_bf16(const uint8_t* data, const uint8_t* scales, void* out,
-                                         int64_t M, int64_t K, int64_t ld_out, cudaStream_t stream)
+                                         int64_t M, int64_t K, int64_t ld_out, cudaStream_t stream,
+                                         uint32_t* zero_words, int n_zero)
 {
     const int64_t nblk = (K + 31) / 32;
     if (M == 0 || K == 0) return cudaSuccess;
@@ -396,10 +407,10 @@ cudaError_t launch_mxfp8_dequantize_bf16(const uint8_t* data, const uint8_t* sca
     if (K % 32 == 0 && ld_out == K && aligned16(out) && (reinterpret_cast<uintptr_t>(data) & 7u) == 0) {
         const int64_t no = M * K / 8;
         mxfp8_dequantize_bf16_flat_kernel<<<codec_grid(no / kPrepassU), kCodecThreads, 0, stream>>>(
-            data, scales, o, no);
+            data, scales, o, no, zero_words, n_zero);
     } else {
         mxfp8_dequantize_bf16_elem_kernel<<<codec_grid(M * K), kCodecThreads, 0, stream>>>(
-            data, scales, o, M, K, nblk, ld_out);
+            data, scales, o, M, K, nblk, ld_out, zero_words, n_zero);
     }
     return cudaGetLastError();
 }

@@ -49,6 +49,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -168,11 +169,31 @@ struct Params {
     int64_t row_offset, col_offset, ldd, lds;
     uint8_t* D_extra[kMaxGatherDest - 1];
     uint8_t* Ds_extra[kMaxGatherDest - 1];
+    // Stream-K (BF16-A kernel; sk_tiles == 0 disables it).  The first sk_tiles tiles
+    // of the raster are not whole work items: their sk_iters = sk_tiles * num_kb
+    // K-steps, taken in raster order, are cut into sk_clusters contiguous ranges,
+    // one per cluster (sk_range_start).  A tile whose K-steps fall into several
+    // ranges is finished by the cluster holding its last K-steps (the owner); the
+    // others (contributors) store their FP32 partial sums into sk_partial (one slot
+    // of kSkSlotFloats per contributing CTA) and count their arrival in sk_sync.
+    // sk_sync[0] hands out the clusters' logical indices in start order; the A
+    // pre-pass zeroes sk_sync[0 .. 1 + 2 * sk_clusters) before the kernel reads it.
+    int sk_tiles, sk_clusters;
+    int64_t sk_iters;
+    float* sk_partial;
+    uint32_t* sk_sync;
 };
 
 // Wait-site ids reported in the device status word.
 enum { kSiteEmpty = 1, kSiteFullB = 2, kSiteFullA16 = 3, kSiteTmemEmpty = 4, kSiteTmemFull = 5,
-       kSiteFullA8 = 6, kSiteEmptyA8 = 7, kSiteEmptyT = 8, kSiteEpiDone = 9, kSiteCopy = 10 };
+       kSiteFullA8 = 6, kSiteEmptyA8 = 7, kSiteEmptyT = 8, kSiteEpiDone = 9, kSiteCopy = 10,
+       kSitePartials = 11 };
+
+// One stream-K partial: a CTA's 128 x 256 FP32 accumulator, stored as
+// [chunk of 32 columns][quad of 4 columns][row][4], so that thread r (row r) of a
+// warp stores and loads consecutive 16-byte pieces.
+constexpr int kSkSlotFloats = BM * BN;
+constexpr uint32_t kSkArrivals = kEpilogueWarps * 32;  // every epilogue thread of a contributing CTA arrives
 
 // Tile order for L2 reuse.  The tile grid is cut into panels of panel_m M tiles;
 // within a panel tiles go M fastest, then N.  The tiles in flight at once (one per
@@ -203,6 +224,154 @@ __device__ __forceinline__ int item_coords(const Params& p, int item, int& m0, i
     tile_coords(p, p.split_from + (j >> 1), m0, n0);
     n0 += (j & 1) * (BN / 2);
     return BN / 2;
+}
+
+// ---------------------------------------------------------------------------
+// Work units of the BF16-A kernel.  Every role of a CTA (producer, MMA issuer,
+// epilogue, copy warps) walks the same sequence: first this cluster's stream-K
+// range, from its last K-step down (so the partial sums other clusters wait for
+// are computed first and the unit this cluster finishes comes last), then whole
+// items strided across the clusters.
+// ---------------------------------------------------------------------------
+enum { kUnitWhole = 0, kUnitContrib = 1, kUnitOwner = 2 };
+
+struct Unit {
+    int m0, n0, bn;     // tile origin and width
+    int kb0, kb1;       // K-steps [kb0, kb1)
+    int kind;           // kUnitWhole: all K-steps; kUnitContrib: store a partial; kUnitOwner: finish the tile
+    int first_contrib;  // owner: clusters first_contrib .. (this cluster - 1) hold the tile's other partials
+};
+
+__device__ __forceinline__ int64_t sk_range_start(const Params& p, int c)
+{
+    return (int64_t)c * p.sk_iters / p.sk_clusters;
+}
+
+struct UnitWalk {
+    int64_t lo, hi;  // stream-K K-steps still to do: [lo, hi), taken from the top
+    int item, stride, cluster;
+
+    __device__ __forceinline__ UnitWalk(const Params& p, int c, int nclusters)
+        : lo(0), hi(0), item(p.sk_tiles + c), stride(nclusters), cluster(c)
+    {
+        if (c < p.sk_clusters) {
+            lo = sk_range_start(p, c);
+            hi = sk_range_start(p, c + 1);
+        }
+    }
+
+    __device__ __forceinline__ bool next(const Params& p, Unit& u)
+    {
+        if (hi > lo) {
+            const int t = (int)((hi - 1) / p.num_kb);
+            const int64_t t0 = (int64_t)t * p.num_kb;  // the tile's first K-step
+            const int64_t b = lo > t0 ? lo : t0;
+            tile_coords(p, t, u.m0, u.n0);
+            u.bn = BN;
+            u.kb0 = (int)(b - t0);
+            u.kb1 = (int)(hi - t0);
+            u.kind = u.kb1 < p.num_kb ? kUnitContrib : (u.kb0 > 0 ? kUnitOwner : kUnitWhole);
+            u.first_contrib = cluster;
+            if (u.kind == kUnitOwner) {
+                // Ranges are contiguous and non-empty: the tile's earlier K-steps lie in
+                // the ranges of clusters cluster-1, cluster-2, ... down to the one whose
+                // range contains t0.  Each of them computes this tile first.
+                int c = cluster - 1;
+                while (c > 0 && sk_range_start(p, c) > t0) --c;
+                u.first_contrib = c;
+            }
+            hi = b;
+            return true;
+        }
+        if (item < p.num_items) {
+            u.bn = item_coords(p, item, u.m0, u.n0);
+            u.kb0 = 0;
+            u.kb1 = p.num_kb;
+            u.kind = kUnitWhole;
+            u.first_contrib = cluster;
+            item += stride;
+            return true;
+        }
+        return false;
+    }
+};
+
+// Partial slot of CTA `rank` of cluster `cluster`.
+__device__ __forceinline__ float4* sk_slot(const Params& p, int cluster, uint32_t rank)
+{
+    return reinterpret_cast<float4*>(p.sk_partial + (size_t)(cluster * 2 + (int)rank) * kSkSlotFloats);
+}
+
+// Owner side: wait until every contributor CTA of this rank has arrived (bounded).
+__device__ __forceinline__ bool sk_wait_partials(const Params& p, int c_first, int c_last, uint32_t rank,
+                                                 volatile int* abort_flag)
+{
+    for (int c = c_last; c >= c_first; --c) {
+        const uint32_t* cnt = p.sk_sync + 1 + 2 * c + (int)rank;
+        if (ld_acquire_gpu(cnt) >= kSkArrivals) continue;
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_gpu(cnt) < kSkArrivals) {
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > p.timeout_ns) {
+                *abort_flag = 1;
+                atomicCAS(p.status, 0, kDevTimeoutBase + kSitePartials);
+                return false;
+            }
+            __nanosleep(128);
+        }
+    }
+    return true;
+}
+
+// Owner side: add the contributors' partial sums (clusters c_first..c_last, in a
+// fixed order: the highest K range first after this CTA's own) into this CTA's
+// accumulator in tensor memory, chunk by chunk, before the ordinary epilogue reads
+// it.  `tacc` is this warp's lane quarter of the accumulator; warp-collective.
+__device__ __noinline__ void sk_merge_partials(const Params& p, uint32_t tacc, int c_first, int c_last,
+                                               uint32_t rank, int r, bool row_ok, int nchunks)
+{
+#pragma unroll 1
+    for (int chunk = 0; chunk < nchunks; ++chunk) {
+        uint32_t raw[32];
+        tmem_ld_32x32b_x32(tacc + 32u * chunk, raw);
+        tmem_ld_wait();
+        if (row_ok) {
+            for (int c = c_last; c >= c_first; --c) {
+                const float4* src = sk_slot(p, c, rank) + (size_t)chunk * 8 * BM + r;
+                float4 x[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) x[q] = __ldcg(src + q * BM);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    raw[4 * q + 0] = __float_as_uint(__uint_as_float(raw[4 * q + 0]) + x[q].x);
+                    raw[4 * q + 1] = __float_as_uint(__uint_as_float(raw[4 * q + 1]) + x[q].y);
+                    raw[4 * q + 2] = __float_as_uint(__uint_as_float(raw[4 * q + 2]) + x[q].z);
+                    raw[4 * q + 3] = __float_as_uint(__uint_as_float(raw[4 * q + 3]) + x[q].w);
+                }
+            }
+        }
+        tmem_st_32x32b_x32(tacc + 32u * chunk, raw);
+    }
+    tmem_st_wait();
+}
+
+// Contributor side: store this CTA's accumulator (this warp's lane quarter `tacc`)
+// as its partial, rows past M skipped; warp-collective.
+__device__ __noinline__ void sk_store_partial(float4* slot_row, uint32_t tacc, bool row_ok, int nchunks)
+{
+#pragma unroll 1
+    for (int c = 0; c < nchunks; ++c) {
+        uint32_t raw[32];
+        tmem_ld_32x32b_x32(tacc + 32u * c, raw);
+        tmem_ld_wait();
+        if (row_ok) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                __stcg(slot_row + (size_t)(c * 8 + q) * BM,
+                       make_float4(__uint_as_float(raw[4 * q]), __uint_as_float(raw[4 * q + 1]),
+                                   __uint_as_float(raw[4 * q + 2]), __uint_as_float(raw[4 * q + 3])));
+        }
+    }
 }
 
 // 16 scale bytes of one row starting at block index b0 (bytes past the row end
@@ -459,9 +628,13 @@ __device__ __forceinline__ void forward_tile(const Params& p, int64_t r0, int nr
     }
 }
 
-// Epilogue of one CTA (4 warps, one thread per accumulator row): for every tile of
-// this cluster, wait for the accumulator, add the dequantized C, quantize D to MXFP8
-// along N and store it, then release the accumulator on rank 0's tempty barrier.
+// Epilogue of one CTA (4 warps, one thread per accumulator row): for every work
+// unit of this cluster (UnitWalk), wait for the accumulator, then
+//   whole tile / stream-K owner: add the contributors' partials (owner), add the
+//     dequantized C, quantize D to MXFP8 along N and store it;
+//   stream-K contributor: store the FP32 accumulator as this CTA's partial and count
+//     this thread's arrival;
+// and release the accumulator on rank 0's tempty barrier.
 template <bool kGather>
 __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base, uint32_t tfull0,
                                          uint32_t tempty_base, int cluster, int nclusters,
@@ -474,14 +647,27 @@ __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base
     const bool has_c = p.C_data != nullptr;
     bool aborted = false;
     int it = 0;
-    for (int item = cluster; item < p.num_items; item += nclusters, ++it) {
-        int m0, n0;
-        const int bn = item_coords(p, item, m0, n0);
+    int published = 0;  // units published to the copy warps (contributor units are not)
+    UnitWalk walk(p, cluster, nclusters);
+    Unit u;
+    for (; walk.next(p, u); ++it) {
+        const int m0 = u.m0, n0 = u.n0, bn = u.bn;
         const int acc = it & 1;
         const uint32_t acc_ph = (uint32_t)(it >> 1) & 1u;
         const int64_t grow = (int64_t)m0 + BM * (int)rank + r;
         const bool row_ok = grow < p.M;
         const int nchunks = min(bn / 32, (p.N - n0 + 31) / 32);
+        const uint32_t tacc = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+        if (u.kind == kUnitContrib) {
+            if (!mbar_wait(tfull(acc), acc_ph, abort_flag, p.status, kSiteTmemFull, p.timeout_ns)) break;
+            tc_fence_after();
+            sk_store_partial(sk_slot(p, cluster, rank) + r, tacc, row_ok, nchunks);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty_base + 8u * acc);
+            red_release_gpu_add(p.sk_sync + 1 + 2 * cluster + (int)rank, 1u);
+            continue;
+        }
         bool full_seen = false;
 #pragma unroll
         for (int c0 = 0; c0 < BN / 32; c0 += kCPrefetch) {
@@ -512,6 +698,14 @@ __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base
                 }
                 tc_fence_after();
                 full_seen = true;
+                if (u.kind == kUnitOwner) {
+                    // The tile's other K ranges: partials of clusters first_contrib .. cluster-1.
+                    if (!sk_wait_partials(p, u.first_contrib, cluster - 1, rank, abort_flag)) {
+                        aborted = true;
+                        break;
+                    }
+                    sk_merge_partials(p, tacc, u.first_contrib, cluster - 1, rank, r, row_ok, nchunks);
+                }
             }
 #pragma unroll
             for (int ci = 0; ci < kCPrefetch; ++ci) {
@@ -558,25 +752,27 @@ __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(tempty_base + 8u * acc);
         if (kGather && tiles_done != nullptr) {
-            // Publish "tile `it` of this CTA is in this GPU's D" to the copy warps:
+            // Publish "this unit's D rows are in this GPU's D" to the copy warps:
             // every epilogue thread arrives (release) after its stores; one thread
             // waits for all 128 (acquire) and bumps the counter the copy warps poll.
             mbar_arrive(epi_done);
             bool ok = true;
             if (quad == 0) {
                 if (lane == 0) {
-                    ok = mbar_wait(epi_done, (uint32_t)it & 1u, abort_flag, p.status, kSiteEpiDone, p.timeout_ns);
+                    ok = mbar_wait(epi_done, (uint32_t)published & 1u, abort_flag, p.status, kSiteEpiDone,
+                                   p.timeout_ns);
                     if (ok) {
                         __threadfence_block();
-                        *tiles_done = it + 1;
+                        *tiles_done = published + 1;
                     }
                 }
                 ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;  // the warp leaves together
             }
             if (!ok) break;
+            ++published;
         }
     }
-    }
+}
 
 __global__ void __maxnreg__(kLaunchRegs)
 gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -887,7 +1083,8 @@ constexpr int P_OFF_BAR = P_OFF_A + P_STAGES * A16_BYTES;
 // barriers: full[S], empty[S], tfull[2], tempty[2], drain, epi_done
 constexpr int P_NUM_BARS = 2 * P_STAGES + 6;
 constexpr int P_OFF_MISC = P_OFF_BAR + P_NUM_BARS * 8;
-constexpr int P_SMEM_BYTES = P_OFF_MISC + 16 + 1024;
+// misc: TMEM address, abort flag, teardown flag, units done (all-gather), cluster ticket
+constexpr int P_SMEM_BYTES = P_OFF_MISC + 32 + 1024;
 static_assert(P_SMEM_BYTES <= 232448, "exceeds the sm_100 per-block shared memory limit");
 static_assert(BK * BN == B_BYTES, "per-stage B bytes of one CTA are BK * item width");
 
@@ -910,12 +1107,13 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + P_OFF_MISC + 4);
     volatile int* never_abort = reinterpret_cast<volatile int*>(smem + P_OFF_MISC + 8);
     volatile int* tiles_done = reinterpret_cast<volatile int*>(smem + P_OFF_MISC + 12);
+    volatile uint32_t* ticket = reinterpret_cast<volatile uint32_t*>(smem + P_OFF_MISC + 16);
     const bool forward = kGather && p.n_extra > 0;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
-    const int cluster = (int)cluster_id_x();
+    int cluster = (int)cluster_id_x();
     const int nclusters = (int)nclusters_x();
 
     if (threadIdx.x == 0) {
@@ -943,6 +1141,22 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
     bool producer_aborted = false;
+    if (p.sk_tiles > 0) {
+        // Stream-K: a cluster waits only for partials of clusters with a lower
+        // logical index, and logical indices are handed out in the order the
+        // clusters start, so every cluster waited for is already running.  The
+        // counter is zeroed by the A pre-pass, which has completed once
+        // wait_for_prerequisite_grid returns.
+        if (rank == 0 && threadIdx.x == 0) {
+            wait_for_prerequisite_grid();
+            const uint32_t tk = atomicAdd(p.sk_sync, 1u);
+            const uint32_t a = smem_u32(const_cast<uint32_t*>(ticket));
+            st_shared_cluster_u32(mapa_shared(a, 0), tk);
+            st_shared_cluster_u32(mapa_shared(a, 1), tk);
+        }
+        cluster_sync_all();
+        cluster = (int)*ticket;
+    }
 
     if (warp == 0) {
         // ------------------------ TMA producer (A and B) -------------------------
@@ -956,14 +1170,14 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
             uint32_t ph = 0;
             int issued = 0;
             bool ok = true;
-            for (int item = cluster; ok && item < p.num_items; item += nclusters) {
-                int m0, n0;
-                const int bn = item_coords(p, item, m0, n0);
-                const int row0 = m0 + BM * (int)rank;
-                const int col0 = n0 + (bn / 2) * (int)rank;
+            UnitWalk walk(p, cluster, nclusters);
+            Unit u;
+            while (ok && walk.next(p, u)) {
+                const int row0 = u.m0 + BM * (int)rank;
+                const int col0 = u.n0 + (u.bn / 2) * (int)rank;
                 // both CTAs' A rows and B columns for one K-step
-                const uint32_t tx = 2u * (uint32_t)(A16_BYTES + BK * bn);
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                const uint32_t tx = 2u * (uint32_t)(A16_BYTES + BK * u.bn);
+                for (int kb = u.kb0; kb < u.kb1; ++kb) {
                     if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, p.status, kSiteEmpty, p.timeout_ns)) {
                         ok = false;
                         break;
@@ -971,7 +1185,7 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
                     if (rank == 0) mbar_arrive_expect_tx(full(s), tx);
                     const uint32_t fb = mapa_shared(full(s), 0);
                     tma_load_2d_pair(sbase + P_OFF_A + s * A16_BYTES, &tmap_a16, fb, kb * BK, row0);
-                    for (int j = 0; j < bn / 128; ++j)
+                    for (int j = 0; j < u.bn / 128; ++j)
                         tma_load_2d_pair(sbase + P_OFF_B + s * B_BYTES + j * B_BOX_BYTES, &tmap_b, fb,
                                          col0 + 64 * j, kb * BK);
                     ++issued;
@@ -996,9 +1210,10 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
             uint32_t ph = 0;
             int it = 0;
             bool ok = true;
-            for (int item = cluster; ok && item < p.num_items; item += nclusters, ++it) {
-                int m0, n0;
-                const uint32_t idesc = item_coords(p, item, m0, n0) == BN ? kIdesc : kIdescHalf;
+            UnitWalk walk(p, cluster, nclusters);
+            Unit u;
+            for (; ok && walk.next(p, u); ++it) {
+                const uint32_t idesc = u.bn == BN ? kIdesc : kIdescHalf;
                 const int acc = it & 1;
                 const uint32_t acc_ph = (uint32_t)(it >> 1) & 1u;
                 if (!mbar_wait(tempty(acc), acc_ph ^ 1u, abort_flag, p.status, kSiteTmemEmpty,
@@ -1008,7 +1223,7 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb = u.kb0; kb < u.kb1; ++kb) {
                     if (!mbar_wait(full(s), ph, abort_flag, p.status, kSiteFullB, p.timeout_ns)) {
                         ok = false;
                         break;
@@ -1020,7 +1235,7 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
                     for (int k = 0; k < BK / UMMA_K; ++k) {
                         const uint64_t adesc = umma_smem_desc_sw128(a_addr + k * UMMA_K * 2, 16, 1024);
                         const uint64_t bdesc = umma_smem_desc_sw128(b_addr + k * UMMA_K * 128, B_BOX_BYTES, 1024);
-                        umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+                        umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb != u.kb0 || k != 0) ? 1u : 0u);
                     }
                     umma_commit_pair_mc(empty(s), 0x3);
                     if (++s == P_STAGES) { s = 0; ph ^= 1u; }
@@ -1039,11 +1254,14 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
         // Forward every tile this CTA's epilogue has finished (tiles_done counts
         // them, in this cluster's tile order) to the other GPUs' full-D buffers.
         const int t = threadIdx.x - 64;
-        int it = 0;
-        for (int item = cluster; item < p.num_items; item += nclusters, ++it) {
+        int published = 0;
+        UnitWalk walk(p, cluster, nclusters);
+        Unit u;
+        while (walk.next(p, u)) {
+            if (u.kind == kUnitContrib) continue;  // no D rows: its owner forwards the tile
             const uint64_t t0 = globaltimer_ns();
             bool ok = true;
-            while (*tiles_done <= it) {
+            while (*tiles_done <= published) {
                 if (*abort_flag) { ok = false; break; }
                 if (globaltimer_ns() - t0 > p.timeout_ns) {
                     *abort_flag = 1;
@@ -1055,12 +1273,11 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
             }
             if (!ok) break;
             __threadfence_block();
-            int m0, n0;
-            const int bn = item_coords(p, item, m0, n0);
-            const int64_t r0 = (int64_t)m0 + BM * (int)rank;
+            ++published;
+            const int64_t r0 = (int64_t)u.m0 + BM * (int)rank;
             const int nrows = (int)min((int64_t)BM, (int64_t)p.M - r0);
-            const int ncols = min(bn, p.N - n0);
-            if (nrows > 0 && ncols > 0) forward_tile(p, r0, nrows, n0, ncols, t, 64);
+            const int ncols = min(u.bn, p.N - u.n0);
+            if (nrows > 0 && ncols > 0) forward_tile(p, r0, nrows, u.n0, ncols, t, 64);
         }
     }
 
@@ -1136,7 +1353,6 @@ namespace {
 
 std::mutex g_mu;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-int* g_status_ptr[64] = {};
 bool g_smem_attr_set[64] = {};
 bool g_regs_checked[64] = {};
 
@@ -1154,19 +1370,19 @@ int get_device(int& dev)
     return MPK_SUCCESS;
 }
 
+// Address of the status word in the current device's context, looked up on every
+// call (a table search once the device code is loaded), so that it is never an
+// address of a context that cudaDeviceReset has destroyed.
 int status_ptr(int dev, int** out)
 {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_status_ptr[dev]) {
-        void* ptr = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&ptr, g_device_status);
-        if (e != cudaSuccess) {
-            set_last_error("cudaGetSymbolAddress(status) failed: %s", cudaGetErrorString(e));
-            return (int)e;
-        }
-        g_status_ptr[dev] = static_cast<int*>(ptr);
+    (void)dev;
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_device_status);
+    if (e != cudaSuccess) {
+        set_last_error("cudaGetSymbolAddress(status) failed: %s", cudaGetErrorString(e));
+        return (int)e;
     }
-    *out = g_status_ptr[dev];
+    *out = static_cast<int*>(ptr);
     return MPK_SUCCESS;
 }
 
@@ -1251,19 +1467,26 @@ int gemm_setup(const uint8_t* A_scales, const void* B, int ldb, const uint8_t* C
     p.ldd = N;
     p.lds = p.nblkN;
     for (int i = 0; i < kMaxGatherDest - 1; ++i) p.D_extra[i] = p.Ds_extra[i] = nullptr;
+    p.sk_tiles = p.sk_clusters = 0;
+    p.sk_iters = 0;
+    p.sk_partial = nullptr;
+    p.sk_sync = nullptr;
     const bool al_c = C_data == nullptr || (reinterpret_cast<uintptr_t>(C_data) & 15u) == 0;
     const bool al_d = (reinterpret_cast<uintptr_t>(D_data) & 15u) == 0;
     p.vec_cd = (N % 16 == 0 && al_c && al_d) ? 1 : 0;
     return MPK_SUCCESS;
 }
 
+// Grid: one cluster per work item up to one per SM pair; at least min_clusters (the
+// stream-K clusters, which need not have whole items).
 template <typename Kernel>
 int launch_pair_kernel(Kernel kernel, int smem_bytes, int threads, const CUtensorMap& tmap_a,
                        const CUtensorMap& tmap_b, const gemm::Params& p, cudaStream_t stream,
-                       bool after_prepass = false)
+                       bool after_prepass = false, int min_clusters = 0)
 {
     const int max_clusters = device_sm_count() / 2;
-    const int clusters = p.num_items < max_clusters ? p.num_items : max_clusters;
+    int clusters = p.num_items < max_clusters ? p.num_items : max_clusters;
+    if (clusters < min_clusters) clusters = min_clusters;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     cfg.blockDim = dim3(threads, 1, 1);
@@ -1281,6 +1504,13 @@ int launch_pair_kernel(Kernel kernel, int smem_bytes, int threads, const CUtenso
     cfg.attrs = attr;
     cfg.numAttrs = after_prepass ? 2 : 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmap_a, tmap_b, p);
+    if (e == cudaErrorInvalidValue || e == cudaErrorLaunchOutOfResources) {
+        // The shared-memory attribute is set once per device; a context re-created
+        // by cudaDeviceReset has lost it.  Set it again and retry once.
+        cudaGetLastError();
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) == cudaSuccess)
+            e = cudaLaunchKernelEx(&cfg, kernel, tmap_a, tmap_b, p);
+    }
     if (e != cudaSuccess) {
         set_last_error("GEMM launch failed: %s", cudaGetErrorString(e));
         return (int)e;
@@ -1311,7 +1541,70 @@ namespace {
 constexpr size_t kWsAlign = 256;
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 int64_t padded8(int x) { return ((int64_t)x + 7) / 8 * 8; }
+
+// Work schedule of the BF16-A kernel (mpk_set_gemm_schedule).
+std::atomic<int> g_schedule{MPK_SCHEDULE_AUTO};
+// A stream-K range shorter than this many 64-wide K-steps costs more in partial
+// traffic and hand-off than it saves.
+constexpr int kSkMinIters = 8;
+
+// Bytes of A's BF16 copy and of B's padded copy (when needed) at the start of the
+// workspace.
+size_t operand_bytes(int M, int N, int K, bool copy_b)
+{
+    size_t bytes = round_up((size_t)M * (size_t)padded8(K) * 2u, kWsAlign);
+    if (copy_b) bytes += (size_t)K * (size_t)padded8(N) * 2u;
+    return bytes;
+}
+
+// Stream-K region after the operands: one partial slot per CTA of the stream-K
+// clusters, then the ticket and arrival counters.
+size_t sk_region_bytes(int sk_clusters)
+{
+    if (sk_clusters <= 0) return 0;
+    return (size_t)sk_clusters * 2u * (size_t)gemm::kSkSlotFloats * 4u +
+           round_up(4u * (1u + 2u * (size_t)sk_clusters), kWsAlign);
+}
 }  // namespace
+
+SkPlan gemm_sk_plan(int M, int N, int K)
+{
+    using namespace gemm;
+    SkPlan plan{0, 0};
+    const int mode = g_schedule.load(std::memory_order_relaxed);
+    if (mode == MPK_SCHEDULE_TILES || M <= 0 || N <= 0 || K <= 0) return plan;
+    const int64_t tiles = (int64_t)((M + PAIR_M - 1) / PAIR_M) * ((N + BN - 1) / BN);
+    const int64_t kb = (K + BK - 1) / BK;
+    const int64_t clusters = device_sm_count() / 2;
+    if (mode == MPK_SCHEDULE_STREAM_K) {
+        // every tile's K-steps spread over all clusters (for tests of the hand-off)
+        plan.tiles = (int)tiles;
+        plan.clusters = (int)std::min(clusters, tiles * kb);
+        return plan;
+    }
+    // Auto: the tiles of the last, partial wave are spread over the clusters when
+    // that gives each cluster at least kSkMinIters K-steps and more clusters than
+    // whole tiles would keep busy.
+    const int64_t rem = tiles % clusters;
+    if (rem == 0) return plan;
+    const int64_t csk = std::min(clusters, rem * kb / kSkMinIters);
+    if (csk <= rem) return plan;
+    plan.tiles = (int)rem;
+    plan.clusters = (int)csk;
+    return plan;
+}
+
+int gemm_set_schedule(int mode)
+{
+    if (mode != MPK_SCHEDULE_AUTO && mode != MPK_SCHEDULE_TILES && mode != MPK_SCHEDULE_STREAM_K) {
+        set_last_error("unknown GEMM schedule %d", mode);
+        return MPK_ERR_INVALID_VALUE;
+    }
+    g_schedule.store(mode);
+    return MPK_SUCCESS;
+}
+
+int gemm_schedule() { return g_schedule.load(); }
 
 int check_onchip_gemm_shape(const uint8_t* A_data, const void* B, int N, int K)
 {
@@ -1334,11 +1627,13 @@ bool gemm_b_needs_copy(const void* B, int N)
     return N % 8 != 0 || (reinterpret_cast<uintptr_t>(B) & 15u) != 0;
 }
 
+size_t gemm_workspace_bytes_min(int M, int N, int K, bool copy_b) { return operand_bytes(M, N, K, copy_b); }
+
 size_t gemm_workspace_bytes(int M, int N, int K, bool copy_b)
 {
-    size_t bytes = round_up((size_t)M * (size_t)padded8(K) * 2u, kWsAlign);
-    if (copy_b) bytes += (size_t)K * (size_t)padded8(N) * 2u;
-    return bytes;
+    const SkPlan plan = gemm_sk_plan(M, N, K);
+    const size_t ops = operand_bytes(M, N, K, copy_b);
+    return plan.tiles > 0 ? round_up(ops, kWsAlign) + sk_region_bytes(plan.clusters) : ops;
 }
 
 int launch_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const void* B,
@@ -1381,7 +1676,7 @@ int launch_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const
 int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scales, const void* B,
                                    const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                                    uint8_t* D_scales, int M, int N, int K, void* workspace,
-                                   cudaStream_t stream, const GatherDest* gather)
+                                   size_t workspace_bytes, cudaStream_t stream, const GatherDest* gather)
 {
     using namespace gemm;
     int dev = 0;
@@ -1432,8 +1727,25 @@ int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scale
             return (int)ce;
         }
     }
-    // Split the last wave's tiles in two when they would fill at most half of it.
-    {
+    // Schedule of the last, partial wave: stream-K when the plan asks for it and the
+    // workspace has room for the partials (never with the fused all-gather); else
+    // split the last wave's tiles in two when they would fill at most half of it.
+    uint32_t* zero_words = nullptr;
+    int n_zero = 0;
+    int min_clusters = 0;
+    const SkPlan plan = gather ? SkPlan{0, 0} : gemm_sk_plan(M, N, K);
+    const size_t sk_off = round_up(operand_bytes(M, N, K, copy_b), kWsAlign);
+    if (plan.tiles > 0 && workspace_bytes >= sk_off + sk_region_bytes(plan.clusters)) {
+        uint8_t* region = static_cast<uint8_t*>(workspace) + sk_off;
+        p.sk_tiles = plan.tiles;
+        p.sk_clusters = plan.clusters;
+        p.sk_iters = (int64_t)plan.tiles * p.num_kb;
+        p.sk_partial = reinterpret_cast<float*>(region);
+        p.sk_sync = reinterpret_cast<uint32_t*>(region + (size_t)plan.clusters * 2u * kSkSlotFloats * 4u);
+        zero_words = p.sk_sync;
+        n_zero = 1 + 2 * plan.clusters;
+        min_clusters = plan.clusters;
+    } else {
         const int tiles = p.num_m_tiles * p.num_n_tiles;
         const int clusters = std::min(tiles, device_sm_count() / 2);
         const int rem = tiles % clusters;
@@ -1442,7 +1754,8 @@ int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scale
             p.num_items = tiles + rem;
         }
     }
-    cudaError_t e = launch_mxfp8_dequantize_bf16(A_data, A_scales, workspace, M, K, lda, stream);
+    cudaError_t e = launch_mxfp8_dequantize_bf16(A_data, A_scales, workspace, M, K, lda, stream, zero_words,
+                                                 n_zero);
     if (e != cudaSuccess) {
         set_last_error("A pre-pass launch failed: %s", cudaGetErrorString(e));
         return (int)e;
@@ -1451,7 +1764,7 @@ int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scale
         return launch_pair_kernel(gemm_bf16a_mxfp8_kernel<true>, P_SMEM_BYTES, P_THREADS, tmap_a16, tmap_b, p,
                                   stream, true);
     return launch_pair_kernel(gemm_bf16a_mxfp8_kernel<false>, P_SMEM_BYTES, P_THREADS, tmap_a16, tmap_b, p,
-                              stream, true);
+                              stream, true, min_clusters);
 }
 
 int launch_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t epoch, cudaStream_t stream)

@@ -19,8 +19,11 @@ cudaError_t launch_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, 
 // MXFP8 [M][K] -> BF16 [M][K] (exact for scale bytes other than 1 and 2).
 cudaError_t launch_mxfp8_quantize_bf16(const void* in, uint8_t* data, uint8_t* scales, int64_t M,
                                        int64_t K, cudaStream_t stream);
+// The GEMM's A pre-pass also zeroes zero_words[0 .. n_zero) (the stream-K ticket and
+// arrival counters of the GEMM kernel launched after it).
 cudaError_t launch_mxfp8_dequantize_bf16(const uint8_t* data, const uint8_t* scales, void* out,
-                                         int64_t M, int64_t K, int64_t ld_out, cudaStream_t stream);
+                                         int64_t M, int64_t K, int64_t ld_out, cudaStream_t stream,
+                                         uint32_t* zero_words = nullptr, int n_zero = 0);
 // D = MXFP8(dequant(C)) along N (C may be null: D = MXFP8(0)).  The K == 0 GEMM.
 cudaError_t launch_mxfp8_requantize(const uint8_t* c_data, const uint8_t* c_scales, uint8_t* d_data,
                                     uint8_t* d_scales, int64_t M, int64_t N, cudaStream_t stream);
@@ -53,11 +56,27 @@ bool gemm_b_needs_copy(const void* B, int N);
 // 0 if `bytes` bytes at ptr lie in memory the current device may store to (an
 // allocation of this device, or a buffer imported on it with mpk_ipc_import).
 int check_store_target(const void* ptr, size_t bytes, const char* what);
+// Workspace of the pre-pass path: gemm_workspace_bytes_min holds A's BF16 copy and
+// B's padded copy; gemm_workspace_bytes adds the stream-K partials when the current
+// schedule uses stream-K for this shape (with less than that the kernel runs whole
+// tiles only).
+size_t gemm_workspace_bytes_min(int M, int N, int K, bool copy_b);
 size_t gemm_workspace_bytes(int M, int N, int K, bool copy_b);
 int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scales, const void* B,
                                    const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                                    uint8_t* D_scales, int M, int N, int K, void* workspace,
-                                   cudaStream_t stream, const GatherDest* gather = nullptr);
+                                   size_t workspace_bytes, cudaStream_t stream,
+                                   const GatherDest* gather = nullptr);
+
+// Stream-K plan of an M x N x K product on the current device under the current
+// schedule: `tiles` tiles (the first of the raster) spread over `clusters` clusters;
+// tiles == 0 means whole tiles only.
+struct SkPlan {
+    int tiles, clusters;
+};
+SkPlan gemm_sk_plan(int M, int N, int K);
+int gemm_set_schedule(int mode);
+int gemm_schedule();
 // Cross-GPU barrier over flag arrays (flags[i]: GPU i's array, at least `world`
 // uint32 slots, peer-accessible); bounded wait, expiry recorded in the status word.
 int launch_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t epoch, cudaStream_t stream);

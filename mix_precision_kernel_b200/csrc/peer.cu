@@ -35,14 +35,15 @@ struct Imported {
     unsigned char handle[sizeof(cudaIpcMemHandle_t)];
 };
 
-std::mutex g_peer_mu;
+std::mutex g_peer_mu;   // guards g_imported
+std::mutex g_range_mu;  // guards g_range_fn
 std::vector<Imported> g_imported;
 PFN_getAddressRange g_range_fn = nullptr;
 
 int address_range(const void* ptr, uintptr_t* base, size_t* size)
 {
     {
-        std::lock_guard<std::mutex> lk(g_peer_mu);
+        std::lock_guard<std::mutex> lk(g_range_mu);
         if (!g_range_fn) {
             void* f = nullptr;
             cudaDriverEntryPointQueryResult q;
@@ -169,9 +170,23 @@ int mpk_ipc_import(const void* handle, uint64_t offset, uint64_t alloc_bytes, vo
         set_last_error("cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
         return (int)e;
     }
+    // The recorded size bounds every later store check, so it is the mapping's real
+    // size, and a caller's size larger than that is refused.
+    uintptr_t mbase = 0;
+    size_t msize = 0;
+    if (int rc = address_range(base, &mbase, &msize)) {
+        cudaIpcCloseMemHandle(base);
+        return rc;
+    }
+    if (mbase != reinterpret_cast<uintptr_t>(base) || alloc_bytes > msize) {
+        cudaIpcCloseMemHandle(base);
+        set_last_error("imported allocation is %zu bytes, not the %llu the exporter described", msize,
+                       (unsigned long long)alloc_bytes);
+        return MPK_ERR_INVALID_VALUE;
+    }
     Imported im;
     im.base = reinterpret_cast<uintptr_t>(base);
-    im.size = alloc_bytes;
+    im.size = msize;
     im.device = dev;
     im.refs = 1;
     std::memcpy(im.handle, handle, sizeof(im.handle));

@@ -38,3 +38,13 @@ def cuda():
     if not torch.cuda.is_available():
         pytest.fail("GPU test collected on a machine without CUDA")
     return torch.device("cuda", 0)
+
+
+@pytest.fixture
+def whole_tiles(mpk_lib):
+    """Runs a test under the whole-tile GEMM schedule (every D element summed in
+    one K order, as the on-chip kernel and any sharding of the same tiles do), and
+    restores the previous schedule afterwards."""
+    prev = mpk_lib.set_gemm_schedule(mpk_lib.SCHEDULE_TILES)
+    yield mpk_lib
+    mpk_lib.set_gemm_schedule(prev)

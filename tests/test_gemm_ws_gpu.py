@@ -7,7 +7,10 @@
   GEMM kernel's own transform warps.
 
 All feed the same BF16 values to the same MMA sequence, so each meets the parity
-bar against the oracle that the default path is held to."""
+bar against the oracle that the default path is held to.  The on-chip kernel runs
+whole tiles only, so it is compared with the pre-pass path under the whole-tile
+schedule; under the default schedule the pre-pass path may split the last wave's
+tiles by K range (stream-K), which sums them in another order."""
 import numpy as np
 import pytest
 
@@ -19,10 +22,21 @@ pytestmark = pytest.mark.gpu
 
 
 def _both(mpk_lib, inp, with_c=True):
+    """D of the default path (default schedule), after checking it against the
+    caller-workspace path (same kernels and schedule: bit for bit) and the on-chip
+    kernel against the pre-pass path under whole tiles (bit for bit)."""
     d0, s0 = run_gemm(mpk_lib, inp, with_c=with_c)
-    for path in ("workspace", "onchip"):
-        d1, s1 = run_gemm(mpk_lib, inp, with_c=with_c, path=path)
-        assert np.array_equal(d0, d1) and np.array_equal(s0, s1), path
+    d1, s1 = run_gemm(mpk_lib, inp, with_c=with_c, path="workspace")
+    assert np.array_equal(d0, d1) and np.array_equal(s0, s1), "workspace"
+    prev = mpk_lib.set_gemm_schedule(mpk_lib.SCHEDULE_TILES)
+    try:
+        dt, st = run_gemm(mpk_lib, inp, with_c=with_c)
+        do, so = run_gemm(mpk_lib, inp, with_c=with_c, path="onchip")
+    finally:
+        mpk_lib.set_gemm_schedule(prev)
+    assert np.array_equal(dt, do) and np.array_equal(st, so), "onchip"
+    hist = O.mx_ulp_hist(d0, s0, dt, st)
+    assert hist[2] == 0 and hist[3] == 0, hist  # schedules differ by summation order only
     return d0, s0
 
 
@@ -141,24 +155,24 @@ def test_pool_release_and_reuse(mpk_lib, cuda):
 
 
 @pytest.mark.parametrize("M,N,K", [(1024, 5120, 256), (2048, 2816, 192)])
-def test_split_tail_tiles_match_onchip(mpk_lib, cuda, M, N, K):
+def test_split_tail_tiles_match_onchip(whole_tiles, cuda, M, N, K):
     """When the last wave would run at most half full, the pre-pass kernel cuts the
     last raster tiles into 256 x 128 halves; D equals the on-chip kernel's (which
     never splits) bit for bit."""
     inp = O.make_gemm_inputs(M, N, K, seed=M + N)
-    d0, s0 = run_gemm(mpk_lib, inp)
-    d1, s1 = run_gemm(mpk_lib, inp, path="onchip")
+    d0, s0 = run_gemm(whole_tiles, inp)
+    d1, s1 = run_gemm(whole_tiles, inp, path="onchip")
     assert np.array_equal(d0, d1) and np.array_equal(s0, s1)
 
 
-def test_split_tail_with_empty_half(mpk_lib, cuda):
+def test_split_tail_with_empty_half(whole_tiles, cuda):
     """N = 2404: the last column of tiles has 100 columns, so the second half of each
     split tile lies past N (no columns to store, accumulator phase still consumed)."""
     M, N, K = 2048, 2404, 64
     inp = O.make_gemm_inputs(M, N, K, seed=7)
-    Dd, Ds = run_gemm(mpk_lib, inp)
+    Dd, Ds = run_gemm(whole_tiles, inp)
     check_parity(Dd, Ds, O.gold_mx(inp), f"split tail {M}x{N}x{K}")
-    assert mpk_lib.device_status() == 0
+    assert whole_tiles.device_status() == 0
 
 
 def test_concurrent_streams_and_threads(mpk_lib, cuda):
