@@ -1,20 +1,27 @@
 """Benchmark of the MXFP8 x BF16 GEMM path (D = A*B + C) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload dense_projection|long_k|tall_skinny|wide|square|codec] [--no-gather]
+                    [--workload dense_projection|long_k|tall_skinny|wide|square|codec]
+                    [--scaling strong|weak] [--no-gather]
 
 One step is one pass of the hot path over one batch of synthetic input: one
-D = A*B + C call at the workload's shape (default: the dense projection
-M=4096, N=12288, K=4096), inputs resident in HBM.  The JSON line's ``value`` is
+D = A*B + C at the workload's shape (default: the dense projection M=4096,
+N=12288, K=4096), inputs resident in HBM.  The JSON line's ``value`` is
 whole-job TFLOP/s (2*M*N*K per GEMM, the reference's formula,
 include/gemm_common.h:30-37) over all ranks; ``e2e`` is the same metric through
-the C ABI with host buffers (pinned host -> device copies of A, B and C, the
-GEMM, device -> host copy of D, every step).
+the C ABI with host buffers (pinned host -> device copies of the step's inputs,
+the GEMM, device -> host copy of D, every step).
 
-Multi-GPU: one process per GPU (torchrun), each rank owns an independent
-M-slab of a GEMM whose total M is N_gpus x the per-rank M (weak scaling, no
-data-path collective; torch.distributed only for the barrier and the max over
-ranks of the timed region).
+Multi-GPU: one process per GPU (torchrun).  Strong scaling (the default): the
+workload's global GEMM is cut into equal slabs, one per rank, with no
+data-path collective -- M-row slabs (B replicated) for the dense projection,
+long-K, tall-skinny and square shapes, N-column slabs of 32-column multiples (A
+replicated) for the wide shape -- so each rank runs 1/N of the FLOPs and
+``value`` is the global FLOPs over the max over ranks of the timed region.
+``--scaling weak`` gives every rank a whole workload-sized slab instead (total
+M = N x M); multi-GPU strong runs also report that figure under ``weak``.
+torch.distributed carries only the barrier, the max over ranks and the optional
+all-gather comparison (``gather``).
 
 ``--impl reference`` times the reference's own CPU implementation of the path
 (gemm_reference_host + mxfp8_quantize_host from oracle/_ref, or the oracle's
@@ -40,12 +47,12 @@ if ROOT not in sys.path:
 
 METRIC = "MXFP8×BF16 GEMM TFLOPS/GPU & % of BF16 TC peak at 1/2/4/8 B200"
 WORKLOADS = {
-    # name: (M per rank, N, K, seed)
-    "dense_projection": (4096, 12288, 4096, 43),
-    "long_k": (4096, 4096, 11008, 44),
-    "tall_skinny": (131072, 2048, 2048, 45),
-    "wide": (2048, 28672, 8192, 46),
-    "square": (16384, 16384, 16384, 46),
+    # name: (M, N, K, seed, how the GEMM is cut across GPUs)
+    "dense_projection": (4096, 12288, 4096, 43, "m"),
+    "long_k": (4096, 4096, 11008, 44, "m"),
+    "tall_skinny": (131072, 2048, 2048, 45, "m"),
+    "wide": (2048, 28672, 8192, 46, "n"),
+    "square": (16384, 16384, 16384, 46, "m"),
 }
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -391,12 +398,62 @@ def make_inputs(mpk, M, N, K, seed, rank):
     return Ad, As, B, Cd, Cs, D, Ds
 
 
+def layout(args, world, rank):
+    """This rank's slab of the workload: (rows, cols, K, M_total, N_total, shards,
+    mode, description).  Strong scaling cuts the workload's global GEMM; weak
+    scaling gives every rank a whole workload-sized M slab."""
+    from mix_precision_kernel_b200 import sharding as S
+
+    M, N, K, _, mode = WORKLOADS[args.workload]
+    if args.scaling == "weak" or world == 1:
+        shards = [S.Shard(r, r * M, (r + 1) * M, 0, N) for r in range(world)]
+        desc = (f"M-slab x{world}, {M} rows per GPU (global M = {M * world}), no collective" if world > 1
+                else "one GPU")
+        return M, N, K, M * world, N, shards, "m", desc
+    shards = S.plan(M, N, world, mode)
+    sh = shards[rank]
+    if mode == "m":
+        desc = f"M-row slabs x{world}: {shards[0].rows} rows per GPU, B replicated, no collective"
+    else:
+        desc = (f"N-column slabs x{world}: {shards[0].cols} columns per GPU (multiples of 32), A replicated, "
+                f"no collective")
+    return sh.rows, sh.cols, K, M, N, shards, mode, desc
+
+
+def workload_config(args, world):
+    """The `config` object both arms print."""
+    M, N, K, seed, _ = WORKLOADS[args.workload]
+    rows, cols, _, M_total, N_total, _, _, desc = layout(args, world, 0)
+    return {"workload": f"{args.workload} GEMM D=A*B+C", "M_total": M_total, "N": N_total, "K": K,
+            "M_per_gpu": rows, "N_per_gpu": cols, "scaling": args.scaling if world > 1 else "single GPU",
+            "A": "MXFP8 e4m3+e8m0/32 along K", "B": "bf16 [K][N]", "C": "MXFP8 along N", "D": "MXFP8 along N",
+            "seed": seed, "parallelism": desc,
+            "l2": f"inputs+outputs per GPU "
+                  f"{((rows * K * 33) // 32 + 2 * K * cols + 2 * (rows * cols * 33) // 32) / 2**20:.0f} MiB; "
+                  f"no flush between steps"}
+
+
+def timed_steps(step, steps, stream, dist):
+    """CUDA-event time of `steps` calls between barriers (ms, this rank)."""
+    import torch
+
+    barrier_sync(dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    barrier_sync(dist)
+    return e0.elapsed_time(e1)
+
+
 def run_gemm_arm(args, world, rank, local, dist):
     import torch
 
     import mix_precision_kernel_b200 as mpk
 
-    M, N, K, seed = WORKLOADS[args.workload]
+    _, _, _, seed, _ = WORKLOADS[args.workload]
+    M, N, K, M_total, N_total, shards, mode, desc = layout(args, world, rank)
     Ad, As, B, Cd, Cs, D, Ds = make_inputs(mpk, M, N, K, seed, rank)
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
@@ -407,7 +464,7 @@ def run_gemm_arm(args, world, rank, local, dist):
     def step():
         rc = L.mpk_gemm_mxfp8_bf16(*a, M, N, K, sptr)
         if rc:
-            raise mpk.MpkError(rc, L.mpk_last_error().decode())
+            raise mpk.MpkError(rc, L.mpk_last_error_string().decode())
 
     for _ in range(args.warmup):
         step()
@@ -429,9 +486,25 @@ def run_gemm_arm(args, world, rank, local, dist):
     ms = e0.elapsed_time(e1)
     assert mpk.device_status() == 0, "device wait expired"
     ms_max = max_over_ranks(dist, ms)
-    flops = 2.0 * M * N * K
+    flops = 2.0 * M * N * K              # this rank's slab
+    flops_job = 2.0 * M_total * N_total * K
     ms_per_step = ms_max / args.steps
-    value = world * flops * args.steps / (ms_max / 1e3) / 1e12
+    value = flops_job * args.steps / (ms_max / 1e3) / 1e12
+    tiles, sk_tiles, sk_pairs = mpk.gemm_plan(M, N, K)
+
+    # Sustained: the same call back to back for at least a second, with its own
+    # clock record (10 ms NVML samples), so the burst figure above can be set
+    # against the clock the power cap allows.
+    sus_steps = max(args.steps, int(1.05e3 / max(ms / args.steps, 1e-3)) + 1)
+    sus_sampler = ClockSampler(gpu_pci_id(local))
+    sus_sampler.start()
+    time.sleep(0.2)
+    barrier_sync(dist)
+    sus_sampler.begin()
+    sus_ms = timed_steps(step, sus_steps, stream, dist)
+    sus_sampler.end()
+    sus_clocks = sus_sampler.stop()
+    sus_ms_max = max_over_ranks(dist, sus_ms)
 
     # A step is two launches on `stream`: the A pre-pass (MXFP8 -> BF16 into the
     # pooled workspace) and the tensor-core kernel.  The pre-pass is timed alone
@@ -440,36 +513,24 @@ def run_gemm_arm(args, world, rank, local, dist):
     pre_args = (Ad.data_ptr(), As.data_ptr(), ws.data_ptr(), M, K, sptr)
     for _ in range(3):
         L.mpk_mxfp8_dequantize_bf16(*pre_args)
-    barrier_sync(dist)
-    e0.record(stream)
-    for _ in range(args.steps):
-        L.mpk_mxfp8_dequantize_bf16(*pre_args)
-    e1.record(stream)
-    barrier_sync(dist)
-    pre_ms = e0.elapsed_time(e1) / args.steps
+    pre_ms = timed_steps(lambda: L.mpk_mxfp8_dequantize_bf16(*pre_args), args.steps, stream, dist) / args.steps
     # Library bar: cuBLAS BF16 x BF16 -> BF16 (torch.matmul) on the same, already
     # dequantized A and B -- a plain GEMM without the C term or the MXFP8 epilogue.
     lib_steps = min(args.steps, 100)
     out16 = torch.matmul(ws, B)
     for _ in range(3):
         torch.matmul(ws, B, out=out16)
-    barrier_sync(dist)
-    e0.record(stream)
-    for _ in range(lib_steps):
-        torch.matmul(ws, B, out=out16)
-    e1.record(stream)
-    barrier_sync(dist)
-    lib_ms = e0.elapsed_time(e1) / lib_steps
+    lib_ms = timed_steps(lambda: torch.matmul(ws, B, out=out16), lib_steps, stream, dist) / lib_steps
     del ws, out16
     gemm_ms = ms / args.steps - pre_ms
     kernel_tflops = flops / (gemm_ms / 1e3) / 1e12
     step_tflops = flops / (ms / args.steps / 1e3) / 1e12
 
     # End to end through the C ABI with host buffers.  Every step uploads all of its
-    # inputs (A, A scales, B, C, C scales) from pinned host memory and downloads its
-    # D and D scales.  Two device buffer sets and three streams (upload, GEMM,
-    # download) let step i+1's upload and step i-1's download run beside step i's
-    # kernels, as a serving loop would pipeline them.
+    # inputs (this rank's A, A scales, B, C, C scales) from pinned host memory and
+    # downloads its D and D scales.  Two device buffer sets and three streams
+    # (upload, GEMM, download) let step i+1's upload and step i-1's download run
+    # beside step i's kernels, as a serving loop would pipeline them.
     hA = torch.empty_like(Ad, device="cpu").pin_memory(); hA.copy_(Ad)
     hAs = torch.empty_like(As, device="cpu").pin_memory(); hAs.copy_(As)
     hB = torch.empty_like(B, device="cpu").pin_memory(); hB.copy_(B)
@@ -502,7 +563,7 @@ def run_gemm_arm(args, world, rank, local, dist):
         rc = L.mpk_gemm_mxfp8_bf16(a_d.data_ptr(), a_s.data_ptr(), b_.data_ptr(), c_d.data_ptr(),
                                    c_s.data_ptr(), d_d.data_ptr(), d_s.data_ptr(), M, N, K, sptr)
         if rc:
-            raise mpk.MpkError(rc, L.mpk_last_error().decode())
+            raise mpk.MpkError(rc, L.mpk_last_error_string().decode())
         ev_used[k].record(stream)
         s_down.wait_event(ev_used[k])
         with torch.cuda.stream(s_down):
@@ -523,16 +584,18 @@ def run_gemm_arm(args, world, rank, local, dist):
     e1.record(stream)
     barrier_sync(dist)
     e2e_ms = max_over_ranks(dist, e0.elapsed_time(e1))
-    e2e_value = world * flops * e2e_steps / (e2e_ms / 1e3) / 1e12
+    e2e_value = flops_job * e2e_steps / (e2e_ms / 1e3) / 1e12
     same = bool(torch.equal(hD[0], hD[1])) and bool(torch.equal(hDs[0].to(D.device), Ds))
     del bufs
+
+    gather = gather_measurement(args, world, rank, dist, mpk, L, M, N, K, M_total, N_total, shards, mode, Ad, As,
+                                B, Cd, Cs, D, Ds, stream) if world > 1 and not args.no_gather else None
+    weak = weak_measurement(args, world, rank, dist, mpk, L, stream) \
+        if world > 1 and args.scaling == "strong" else None
 
     # Denominator: the burst cuBLAS figure, unless the clock record shows the power
     # cap acting during the timed region, in which case the sustained figure (the
     # same GEMM measured back to back under the cap).  Both fractions are reported.
-    gather = gather_measurement(args, world, rank, dist, mpk, L, M, N, K, Ad, As, B, Cd, Cs, D, Ds, stream) \
-        if world > 1 and not args.no_gather else None
-
     peaks, peak_src = load_peaks()
     burst = float(peaks["bf16_tflops"])
     sustained = float(peaks.get("bf16_tflops_sustained", burst))
@@ -543,34 +606,38 @@ def run_gemm_arm(args, world, rank, local, dist):
     roofline = {"bound": "tensor", "kernel": "gemm_bf16a_mxfp8_kernel",
                 "achieved": round(kernel_tflops, 2), "peak": peak,
                 "unit": "TFLOP/s", "frac": round(kernel_tflops / peak, 4),
-                "traffic": load_traffic("gemm_bf16a_mxfp8_kernel", args.workload),
+                "traffic": load_traffic("gemm_bf16a_mxfp8_kernel", args.workload) if world == 1 else None,
                 "peak_source": (f"{peak_src} bf16_tflops_sustained (sw_power_cap active in the timed "
                                 f"region)" if capped else f"{peak_src} bf16_tflops (burst)"),
                 "frac_of_burst": round(kernel_tflops / burst, 4),
-                "algorithmic": f"2*M*N*K = {flops:.4e} FLOP per launch",
+                "frac_of_sustained": round(kernel_tflops / sustained, 4),
+                "algorithmic": f"2*M*N*K = {flops:.4e} FLOP per launch (this GPU's slab {M}x{N}x{K})",
                 "kernel_ms": round(gemm_ms, 5),
                 "timing": "step time (CUDA events over the timed region) minus the A pre-pass "
                           "timed alone over the same number of launches",
+                "schedule": {"tiles": tiles, "stream_k_tiles": sk_tiles, "stream_k_pairs": sk_pairs},
                 "step_achieved": round(step_tflops, 2), "step_frac": round(step_tflops / peak, 4),
                 "prepass": {"kernel": "mxfp8_dequantize_bf16_flat_kernel", "ms": round(pre_ms, 5),
                             "bytes": pre_bytes, "achieved_gbs": round(pre_bytes / pre_ms / 1e6, 1),
                             "frac_of_hbm": round(pre_bytes / pre_ms / 1e6 / hbm, 4)}}
+    nv = clocks.get("nvml") or {}
+    snv = sus_clocks.get("nvml") or {}
+    sus_tflops = flops_job * sus_steps / (sus_ms_max / 1e3) / 1e12
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": args.scaling if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "bf16",
         "data": "synthetic (N(0,0.02^2) drawn on device, torch Philox seeded; A/C quantized to "
                 "MXFP8 by the library, B rounded to BF16)",
-        "config": {"workload": f"{args.workload} GEMM D=A*B+C", "M_per_gpu": M, "M_total": M * world,
-                   "N": N, "K": K, "A": "MXFP8 e4m3+e8m0/32 along K", "B": "bf16 [K][N]",
-                   "C": "MXFP8 along N", "D": "MXFP8 along N", "seed": seed,
-                   "parallelism": f"M-slab x{world}, no collective",
-                   "l2": f"inputs+outputs {((M*K*33)//32 + 2*K*N + 2*(M*N*33)//32)/2**20:.0f} MiB > "
-                         f"126 MiB L2; no flush between steps"},
+        "config": workload_config(args, world),
+        "tflops_per_gpu": round(value / world, 2),
         "gpu_launches": 2 * args.steps,
         "pct_of_bf16_peak": round(100.0 * value / world / burst, 2),
-        "e2e": {"value": round(e2e_value, 3), "unit": "TFLOPS", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "steps": e2e_steps, "ms_per_step": round(e2e_ms / e2e_steps, 4),
+        "e2e": {"value": round(e2e_value, 3), "unit": "TFLOPS",
+                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+                "h2d_bytes_per_step_per_gpu": h2d, "d2h_bytes_per_step_per_gpu": d2h,
+                "steps": e2e_steps, "ms_per_step": round(e2e_ms / e2e_steps, 4),
                 "pipelining": "two buffer sets; upload, GEMM and download streams overlap across steps",
                 "downloads_match_device_result": same},
         "roofline": roofline,
@@ -580,6 +647,17 @@ def run_gemm_arm(args, world, rank, local, dist):
                         "gemm_kernel_over_library": round(lib_ms / gemm_ms, 4),
                         "step_over_library": round(lib_ms / (ms / args.steps), 4)},
         "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+        "sustained": {"what": "the same call back to back for >= 1 s with a 10 ms NVML clock record",
+                      "steps": sus_steps, "ms_per_step": round(sus_ms_max / sus_steps, 5),
+                      "value": round(sus_tflops, 2),
+                      "frac_of_sustained_peak": round(sus_tflops / world / sustained, 4),
+                      "frac_of_burst_peak": round(sus_tflops / world / burst, 4),
+                      "sm_mhz_median": snv.get("sm_mhz_median"), "samples": snv.get("samples"),
+                      "in_timed_region": snv.get("in_timed_region"), "reasons": sus_clocks["reasons"],
+                      "ms_x_ghz": (round(sus_ms_max / sus_steps * snv["sm_mhz_median"] / 1e3, 5)
+                                   if snv.get("sm_mhz_median") else None)},
+        "burst_ms_x_ghz": (round(ms_per_step * nv["sm_mhz_median"] / 1e3, 5)
+                           if nv.get("sm_mhz_median") else None),
     }
     line["clocks"]["samples"] = clocks["samples"]
     line["clocks"]["in_timed_region"] = clocks.get("in_timed_region")
@@ -594,57 +672,126 @@ def run_gemm_arm(args, world, rank, local, dist):
     line["clocks"]["nvml_10ms"] = clocks.get("nvml")
     if gather is not None:
         line["gather"] = gather
+    if weak is not None:
+        line["weak"] = weak
+    if world == 1 and rank == 0 and not args.no_reference_gpu:
+        line["reference_gpu_bar"] = reference_gpu_bar(Ad, As, B, Cd, Cs, M, N, K, ms / args.steps)
     return line
 
 
-def gather_measurement(args, world, rank, dist, mpk, L, M, N, K, Ad, As, B, Cd, Cs, D, Ds, stream):
-    """GEMM + all-gather of D onto every GPU, two ways, over the same M slabs: the
+def weak_measurement(args, world, rank, dist, mpk, L, stream):
+    """Weak scaling beside a strong run: every rank runs a whole workload-sized
+    GEMM of its own (an independent M slab); whole-job TFLOP/s, max over ranks."""
+    import torch
+
+    M, N, K, seed, _ = WORKLOADS[args.workload]
+    Ad, As, B, Cd, Cs, D, Ds = make_inputs(mpk, M, N, K, seed + 7, rank)
+    a = [Ad.data_ptr(), As.data_ptr(), B.data_ptr(), Cd.data_ptr(), Cs.data_ptr(), D.data_ptr(), Ds.data_ptr()]
+    sptr = stream.cuda_stream
+
+    def step():
+        rc = L.mpk_gemm_mxfp8_bf16(*a, M, N, K, sptr)
+        if rc:
+            raise mpk.MpkError(rc, L.mpk_last_error_string().decode())
+
+    steps = max(5, min(args.steps, 50))
+    for _ in range(3):
+        step()
+    ms = max_over_ranks(dist, timed_steps(step, steps, stream, dist))
+    del Ad, As, B, Cd, Cs, D, Ds
+    torch.cuda.empty_cache()
+    value = world * 2.0 * M * N * K * steps / (ms / 1e3) / 1e12
+    return {"what": f"weak scaling: {M}x{N}x{K} on every GPU (global M = {M * world})",
+            "value": round(value, 2), "tflops_per_gpu": round(value / world, 2),
+            "ms_per_step": round(ms / steps, 5), "steps": steps}
+
+
+def reference_gpu_bar(Ad, As, B, Cd, Cs, M, N, K, our_step_ms):
+    """The reference's own GPU launcher (gemm_fp8_tensorcore: WMMA fp16 into an FP32
+    temporary, then its quantize kernel; src/kernels/gemm_fp8_tensorcore.cu:231-249),
+    rebuilt for sm_100a in oracle/_ref, on the same device inputs: a baseline
+    measurement beside ours, like the CPU baseline."""
+    import torch
+
+    import oracle as O
+
+    if not O.ref_available():
+        return {"unavailable": "oracle/_ref (the reference compiled here) is not built"}
+    R = O.ref()
+    D7 = torch.empty((M, N), dtype=torch.uint8, device="cuda")
+    S7 = torch.empty((M, (N + 31) // 32), dtype=torch.uint8, device="cuda")
+    args = (Ad.data_ptr(), As.data_ptr(), B.data_ptr(), Cd.data_ptr(), Cs.data_ptr(), D7.data_ptr(),
+            S7.data_ptr(), M, N, K, None)
+    assert R.ref_gemm_fp8_tensorcore(*args) == 0
+    torch.cuda.synchronize()
+    n = 3
+    t0 = time.perf_counter()
+    for _ in range(n):
+        assert R.ref_gemm_fp8_tensorcore(*args) == 0
+    torch.cuda.synchronize()
+    ms = (time.perf_counter() - t0) / n * 1e3
+    tflops = 2.0 * M * N * K / (ms / 1e3) / 1e12
+    del D7, S7
+    return {"what": "the reference's gemm_fp8_tensorcore (WMMA fp16 + FP32 temporary + quantize kernel, "
+                    "per-call cudaMalloc/cudaFree) rebuilt for sm_100a, same inputs, same GPU",
+            "ms": round(ms, 4), "tflops": round(tflops, 3), "calls": n,
+            "timing": "host wall clock around synchronous calls (the launcher synchronizes on its "
+                      "cudaMalloc/cudaFree)",
+            "our_step_over_reference": round(ms / our_step_ms, 2)}
+
+
+def gather_measurement(args, world, rank, dist, mpk, L, M, N, K, M_total, N_total, shards, mode, Ad, As, B, Cd,
+                       Cs, D, Ds, stream):
+    """GEMM + all-gather of D onto every GPU, two ways, over this run's slabs: the
     fused kernel (each D tile stored into every GPU's full-D buffer by the epilogue,
-    then a cross-GPU barrier) and the GEMM followed by NCCL all_gather_into_tensor
-    of D and its scales.  Times are max over ranks."""
+    then a cross-GPU barrier) and the GEMM followed by NCCL all-gathers of D and
+    its scales.  Both run whole tiles (the fused kernel has no stream-K schedule),
+    so their results must be identical.  Times are max over ranks."""
     import torch
 
     from mix_precision_kernel_b200 import sharding as S
 
-    M_total = M * world
-    shards = S.plan(M_total, N, world, "m")
-    gg = S.GatherGemm(M_total, N, K, shards, None)
-    fullD = torch.empty((M_total, N), dtype=torch.uint8, device="cuda")
-    fullS = torch.empty((M_total, (N + 31) // 32), dtype=torch.uint8, device="cuda")
-    steps = max(5, min(args.steps, 50))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    prev = mpk.set_gemm_schedule(mpk.SCHEDULE_TILES)
+    try:
+        gg = S.GatherGemm(M_total, N_total, K, shards, None)
+        steps = max(5, min(args.steps, 50))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        gathered = {}
 
-    def fused():
-        gg(Ad, As, B, Cd, Cs)
+        def fused():
+            gg(Ad, As, B, Cd, Cs)
 
-    def separate():
-        rc = L.mpk_gemm_mxfp8_bf16(Ad.data_ptr(), As.data_ptr(), B.data_ptr(), Cd.data_ptr(), Cs.data_ptr(),
-                                   D.data_ptr(), Ds.data_ptr(), M, N, K, stream.cuda_stream)
-        if rc:
-            raise mpk.MpkError(rc, L.mpk_last_error().decode())
-        dist.all_gather_into_tensor(fullD, D)
-        dist.all_gather_into_tensor(fullS, Ds)
+        def separate():
+            rc = L.mpk_gemm_mxfp8_bf16(Ad.data_ptr(), As.data_ptr(), B.data_ptr(), Cd.data_ptr(), Cs.data_ptr(),
+                                       D.data_ptr(), Ds.data_ptr(), M, N, K, stream.cuda_stream)
+            if rc:
+                raise mpk.MpkError(rc, L.mpk_last_error_string().decode())
+            gathered["d"], gathered["s"] = S.gather_d(D, Ds, shards, mode)
 
-    out = {}
-    for name, fn in (("separate", separate), ("fused", fused)):
-        for _ in range(3):
-            fn()
-        barrier_sync(dist)
-        e0.record(stream)
-        for _ in range(steps):
-            fn()
-        e1.record(stream)
-        barrier_sync(dist)
-        out[name] = max_over_ranks(dist, e0.elapsed_time(e1) / steps)
-    same = bool(torch.equal(gg.D, fullD)) and bool(torch.equal(gg.Ds, fullS))
-    ok = torch.tensor([1 if same else 0], device="cuda")
-    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-    gg.close()
+        out = {}
+        for name, fn in (("separate", separate), ("fused", fused)):
+            for _ in range(3):
+                fn()
+            barrier_sync(dist)
+            e0.record(stream)
+            for _ in range(steps):
+                fn()
+            e1.record(stream)
+            barrier_sync(dist)
+            out[name] = max_over_ranks(dist, e0.elapsed_time(e1) / steps)
+        same = bool(torch.equal(gg.D, gathered["d"])) and bool(torch.equal(gg.Ds, gathered["s"]))
+        ok = torch.tensor([1 if same else 0], device="cuda")
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        gg.close()
+    finally:
+        mpk.set_gemm_schedule(prev)
     d_bytes = M * N + M * ((N + 31) // 32)
-    return {"what": "D = A*B + C on M slabs, then D and its scales on every GPU",
+    return {"what": f"D = A*B + C on {'M-row' if mode == 'm' else 'N-column'} slabs, then D and its scales "
+                    f"on every GPU",
             "fused_ms": round(out["fused"], 5), "separate_ms": round(out["separate"], 5),
             "speedup": round(out["separate"] / out["fused"], 3),
-            "separate": "mpk GEMM + NCCL all_gather_into_tensor (D, scales)",
+            "separate": "mpk GEMM + NCCL all-gather of D and scales (all_gather_into_tensor for equal row "
+                        "slabs, all_gather + reassembly for column slabs)",
             "fused": "GEMM epilogue stores every tile into all GPUs' full-D buffers (peer stores), "
                      "cross-GPU barrier before and after",
             "bytes_sent_per_gpu": d_bytes * (world - 1),
@@ -814,29 +961,40 @@ def run_reference_arm(args, world, rank):
         return None
     if args.workload == "codec":
         return run_reference_codec_arm(args, world)
-    M, N, K, seed = WORKLOADS[args.workload]
-    # Each step is a bounded row sample; the per-step budget shrinks with the step
-    # count so that the whole run stays within about two minutes of host work.
+    M, N, K, seed, _ = WORKLOADS[args.workload]
+    # Each step is one timed row sample of the whole workload (rows are independent,
+    # so the sample's throughput is the workload's); the per-step budget shrinks with
+    # the step count so that the whole run stays within about two minutes of host
+    # work.  The metric is a rate, so the sample gives it without extrapolation;
+    # the time a whole workload-sized step would take is reported beside it.
     budget = float(os.environ.get("MPK_REF_STEP_BUDGET_S", "2.0"))
     budget = max(0.05, min(budget, 120.0 / (args.steps + args.warmup)))
     cb = CpuBaseline(M, N, K, seed)
     cb.calibrate(budget, seed + 1)
-    vals = []
+    vals, secs = [], []
     desc = None
     for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
         v, desc = cb.sample(seed + 2 + i)
         if i >= args.warmup:
             vals.append(v)
+            secs.append(time.perf_counter() - t0)
     value = statistics.mean(vals)
     desc = dict(desc, value=value)
     desc["cpu_model"] = cpu_model()
+    sample_rows = cb.threads * cb.rows
+    full_ms = 2.0 * M * N * K / (value * 1e12) * 1e3
+    # The whole job at N GPUs is the same global workload (strong scaling) or N of
+    # them (weak); the host cores run it once either way.
     return {
         "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 2.0 * M * N * K / (value * 1e12) * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic N(0,0.02^2)", "impl": "reference",
-        "config": {"workload": f"{args.workload} GEMM D=A*B+C", "M_per_gpu": M, "N": N, "K": K,
-                   "parallelism": "host threads, row slabs"},
+        "warmup": args.warmup, "ms_per_step": round(statistics.mean(secs) * 1e3, 3),
+        "higher_is_better": True, "scaling": args.scaling if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic N(0,0.02^2)", "impl": "reference",
+        "config": workload_config(args, world),
+        "step": f"one timed sample of {sample_rows} rows of the {M}x{N}x{K} workload on {cb.threads} host threads",
+        "extrapolated": True, "sample_rows": sample_rows, "sample_s": round(statistics.mean(secs), 4),
+        "full_step_ms_extrapolated": round(full_ms, 1),
         "cpu_baseline": desc,
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
@@ -855,7 +1013,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gather", action="store_true",
                     help="with --gpus > 1: skip timing the fused GEMM + all-gather of D against the GEMM "
-                         "followed by NCCL all_gather_into_tensor (reported as `gather`)")
+                         "followed by NCCL all-gathers (reported as `gather`)")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="strong: the workload's global GEMM is split over the GPUs (default); weak: every "
+                         "GPU runs a whole workload-sized M slab")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own GPU launcher beside ours (reference_gpu_bar)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -878,7 +1041,7 @@ def main():
                 sub = argparse.Namespace(steps=3, warmup=1)
                 line["cpu_baseline"] = run_reference_codec_arm(sub, 1)["cpu_baseline"]
             else:
-                M, N, K, seed = WORKLOADS[args.workload]
+                M, N, K, seed, _ = WORKLOADS[args.workload]
                 _, desc = cpu_baseline(M, N, K, seed, args.cpu_budget_s)
                 desc["cpu_model"] = cpu_model()
                 line["cpu_baseline"] = desc

@@ -203,6 +203,23 @@ int mpk_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, float* outp
 int mpk_mxfp8_quantize_bf16(const void* input, uint8_t* data, uint8_t* scales, int M, int K,
                             void* stream);
 
+/* float [M][K] (row-major) -> MXFP8 with the blocks along the rows: each column is
+ * cut into blocks of 32 consecutive rows (the last one partial when M % 32 != 0),
+ * each with one E8M0 scale.  data is [M][K] (the input's layout), scales are
+ * [ceil(M/32)][K] row-major, scale of rows [32b, 32b+32) of column k at b*K + k.
+ * The reference's quantize rule (src/quantize/mxfp8_quantize.cu:7-42) with the
+ * block axis chosen: bit-exact with mpk_mxfp8_quantize applied to the transposed
+ * tensor, transposed back.  For producers whose blocks run along the strided axis
+ * (an activation stored [K][M] for an A operand, or a C built column-wise).  Any
+ * M, K >= 0; input 4-byte aligned.  No counterpart in the reference (its quantizer
+ * blocks along the contiguous axis only). */
+int mpk_mxfp8_quantize_cols(const float* input, uint8_t* data, uint8_t* scales, int M, int K, void* stream);
+
+/* BF16 [M][K] (bit patterns, 2-byte aligned) -> MXFP8 with the blocks along the
+ * rows, as mpk_mxfp8_quantize_cols on each value widened exactly to FP32.  No
+ * counterpart in the reference. */
+int mpk_mxfp8_quantize_bf16_cols(const void* input, uint8_t* data, uint8_t* scales, int M, int K, void* stream);
+
 /* MXFP8 [M][K] -> BF16 [M][K] (bit patterns, 2-byte aligned output): code x
  * 2^(scale-127) rounded to nearest even, which is exact for scale bytes >= 3.
  * This is the A pre-pass of mpk_gemm_mxfp8_bf16.  No counterpart in the reference

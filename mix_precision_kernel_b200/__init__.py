@@ -28,6 +28,7 @@ __all__ = [
     "mxfp8_quantize_host", "mxfp8_dequantize_host",
     "gemm_fp8_tensorcore_ws", "gemm_workspace_size", "release_workspace_pool",
     "mxfp8_dequantize_bf16_gpu", "mxfp8_quantize_bf16_gpu", "gemm_fp8_tensorcore_gather", "peer_barrier",
+    "mxfp8_quantize_cols_gpu", "mxfp8_quantize_bf16_cols_gpu", "quantize_cols",
     "ipc_export", "ipc_import", "ipc_close",
     "gemm_fp8_tensorcore_noalloc", "NOALLOC_SCRATCH_BYTES",
     "gemm", "quantize", "dequantize", "device_status", "set_wait_timeout_ns", "wait_selftest",
@@ -89,6 +90,8 @@ def lib() -> ctypes.CDLL:
             L.mpk_mxfp8_dequantize.argtypes = [vp, vp, vp, ci, ci, vp]
             L.mpk_mxfp8_dequantize_bf16.argtypes = [vp, vp, vp, ci, ci, vp]
             L.mpk_mxfp8_quantize_bf16.argtypes = [vp, vp, vp, ci, ci, vp]
+            L.mpk_mxfp8_quantize_cols.argtypes = [vp, vp, vp, ci, ci, vp]
+            L.mpk_mxfp8_quantize_bf16_cols.argtypes = [vp, vp, vp, ci, ci, vp]
             L.mpk_gemm_mxfp8_bf16_gather.argtypes = [vp, vp, vp, vp, vp, ci, ci, ci, ctypes.c_int64,
                                                      ctypes.c_int64, ci, ci, vp, vp, ci, vp, ctypes.c_size_t,
                                                      vp]
@@ -115,6 +118,7 @@ def lib() -> ctypes.CDLL:
                       "mpk_release_workspace_pool", "mpk_mxfp8_quantize", "mpk_mxfp8_dequantize",
                       "mpk_mxfp8_dequantize_bf16", "mpk_gemm_mxfp8_bf16_noalloc",
                       "mpk_mxfp8_quantize_bf16", "mpk_gemm_mxfp8_bf16_gather", "mpk_peer_barrier",
+                      "mpk_mxfp8_quantize_cols", "mpk_mxfp8_quantize_bf16_cols",
                       "mpk_ipc_export", "mpk_ipc_import", "mpk_ipc_close",
                       "mpk_mxfp8_quantize_host", "mpk_mxfp8_dequantize_host", "mpk_device_status",
                       "mpk_set_wait_timeout_ns", "mpk_wait_selftest", "mpk_version",
@@ -280,6 +284,31 @@ def mxfp8_quantize_bf16_gpu(input, data, scales, M: int, K: int, stream=None) ->
     """BF16 [M, K] -> MXFP8 along K (each value widened exactly to FP32 first)."""
     s = _stream(stream, input, data)
     _check(lib().mpk_mxfp8_quantize_bf16(_addr(input), _addr(data), _addr(scales), M, K, s))
+
+
+def mxfp8_quantize_cols_gpu(input, data, scales, M: int, K: int, stream=None) -> None:
+    """float32 [M, K] -> MXFP8 with blocks of 32 rows per column: data [M, K], scales
+    [ceil(M/32), K]."""
+    s = _stream(stream, input, data)
+    _check(lib().mpk_mxfp8_quantize_cols(_addr(input), _addr(data), _addr(scales), M, K, s))
+
+
+def mxfp8_quantize_bf16_cols_gpu(input, data, scales, M: int, K: int, stream=None) -> None:
+    """BF16 [M, K] -> MXFP8 with blocks of 32 rows per column (values widened exactly)."""
+    s = _stream(stream, input, data)
+    _check(lib().mpk_mxfp8_quantize_bf16_cols(_addr(input), _addr(data), _addr(scales), M, K, s))
+
+
+def quantize_cols(x, stream=None):
+    """float32 or bfloat16 CUDA tensor [M, K] -> (codes uint8 [M, K], scales uint8
+    [ceil(M/32), K]), blocks of 32 rows per column."""
+    import torch
+    assert x.is_cuda and x.dim() == 2 and x.is_contiguous() and x.dtype in (torch.float32, torch.bfloat16)
+    M, K = x.shape
+    d = torch.empty((M, K), dtype=torch.uint8, device=x.device)
+    s = torch.empty((nblk(M), K), dtype=torch.uint8, device=x.device)
+    (mxfp8_quantize_cols_gpu if x.dtype == torch.float32 else mxfp8_quantize_bf16_cols_gpu)(x, d, s, M, K, stream)
+    return d, s
 
 
 def mxfp8_dequantize_bf16_gpu(data, scales, output, M: int, K: int, stream=None) -> None:

@@ -491,6 +491,47 @@ int mpk_mxfp8_quantize_bf16(const void* input, uint8_t* data, uint8_t* scales, i
                      "quantize-bf16 launch");
 }
 
+static int validate_cols(const void* input, const uint8_t* data, const uint8_t* scales, int M, int K,
+                         size_t elem_bytes, bool& nothing_to_do)
+{
+    nothing_to_do = false;
+    if (M < 0 || K < 0) {
+        set_last_error("negative size M=%d K=%d", M, K);
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (M == 0 || K == 0) {
+        nothing_to_do = true;
+        return MPK_SUCCESS;
+    }
+    if (!input || !data || !scales) {
+        set_last_error("null device pointer");
+        return MPK_ERR_INVALID_VALUE;
+    }
+    if (reinterpret_cast<uintptr_t>(input) % elem_bytes) {
+        set_last_error("input must be %zu-byte aligned", elem_bytes);
+        return MPK_ERR_MISALIGNED;
+    }
+    return check_arch();
+}
+
+int mpk_mxfp8_quantize_cols(const float* input, uint8_t* data, uint8_t* scales, int M, int K, void* stream)
+{
+    bool done = false;
+    if (int rc = validate_cols(input, data, scales, M, K, 4, done)) return rc;
+    if (done) return MPK_SUCCESS;
+    return from_cuda(launch_mxfp8_quantize_cols(input, data, scales, M, K, (cudaStream_t)stream),
+                     "column quantize launch");
+}
+
+int mpk_mxfp8_quantize_bf16_cols(const void* input, uint8_t* data, uint8_t* scales, int M, int K, void* stream)
+{
+    bool done = false;
+    if (int rc = validate_cols(input, data, scales, M, K, 2, done)) return rc;
+    if (done) return MPK_SUCCESS;
+    return from_cuda(launch_mxfp8_quantize_bf16_cols(input, data, scales, M, K, (cudaStream_t)stream),
+                     "column quantize-bf16 launch");
+}
+
 int mpk_mxfp8_dequantize_bf16(const uint8_t* data, const uint8_t* scales, void* output, int M, int K,
                               void* stream)
 {

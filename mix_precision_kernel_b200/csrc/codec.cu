@@ -334,6 +334,89 @@ mxfp8_dequantize_bf16_elem_kernel(const uint8_t* __restrict__ data, const uint8_
     }
 }
 
+// ------------------------- quantize along the rows --------------------------
+// MXFP8 with the block axis along the strided dimension: each column of a
+// row-major [M][K] tensor is cut into blocks of 32 consecutive rows, each with one
+// E8M0 scale; codes keep the input's layout ([M][K]) and the scales are
+// [ceil(M/32)][K] row-major.  The arithmetic is the reference's per-block rule
+// (src/quantize/mxfp8_quantize.cu:7-42: amax with NaN ignored, E8M0 = round-up
+// power of two of amax / 448, RNE E4M3 of x / scale), so the result is the row
+// quantizer's on the transposed tensor, transposed back.
+//
+// One thread per (32-row block, group of kCols columns); consecutive threads take
+// consecutive column groups, so each of the 32 row loads of a warp reads one
+// contiguous span (512 B of FP32 with 4 columns per thread) and each code store
+// writes one (128 B).  All 32 rows are loaded before any arithmetic.
+constexpr int kColsThreads = 128;
+
+template <typename T, int kCols>
+__device__ __forceinline__ void load_cols(const T* p, float (&v)[kCols])
+{
+    if constexpr (kCols == 4 && sizeof(T) == 4) {
+        const float4 x = __ldcs(reinterpret_cast<const float4*>(p));
+        v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+    } else if constexpr (kCols == 4) {
+        const uint2 x = __ldcs(reinterpret_cast<const uint2*>(p));
+        v[0] = __uint_as_float(x.x << 16); v[1] = __uint_as_float(x.x & 0xFFFF0000u);
+        v[2] = __uint_as_float(x.y << 16); v[3] = __uint_as_float(x.y & 0xFFFF0000u);
+    } else {
+#pragma unroll
+        for (int c = 0; c < kCols; ++c) v[c] = load_elem(p + c);
+    }
+}
+
+template <typename T, int kCols>
+__global__ void __launch_bounds__(kColsThreads)
+mxfp8_quantize_cols_kernel(const T* __restrict__ in, uint8_t* __restrict__ data, uint8_t* __restrict__ scales,
+                           int64_t M, int64_t K, int64_t ngroups, int64_t nblocks)
+{
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; w < ngroups * nblocks; w += stride) {
+        const int64_t k0 = (w % ngroups) * kCols;
+        const int64_t r0 = (w / ngroups) * 32;
+        const int rows = (int)min((int64_t)32, M - r0);
+        float v[32][kCols];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            if (i < rows) {
+                load_cols<T, kCols>(in + (r0 + i) * K + k0, v[i]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < kCols; ++c) v[i][c] = 0.0f;
+            }
+        }
+        float inv[kCols];
+        uint32_t sc = 0u;
+#pragma unroll
+        for (int c = 0; c < kCols; ++c) {
+            float amax = 0.0f;  // NaN elements ignored; rows past M contribute 0
+#pragma unroll
+            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i][c]));
+            sc |= mx_block_scale(amax, inv[c]) << (8 * c);
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            if (i >= rows) break;
+            uint8_t* dst = data + (r0 + i) * K + k0;
+            if constexpr (kCols == 4) {
+                const uint32_t c01 = f32x2_to_e4m3x2(v[i][0] * inv[0], v[i][1] * inv[1]);
+                const uint32_t c23 = f32x2_to_e4m3x2(v[i][2] * inv[2], v[i][3] * inv[3]);
+                __stcs(reinterpret_cast<uint32_t*>(dst), c01 | (c23 << 16));
+            } else {
+#pragma unroll
+                for (int c = 0; c < kCols; ++c) dst[c] = (uint8_t)f32x2_to_e4m3x2(v[i][c] * inv[c], 0.0f);
+            }
+        }
+        uint8_t* sdst = scales + (r0 / 32) * K + k0;
+        if constexpr (kCols == 4) {
+            *reinterpret_cast<uint32_t*>(sdst) = sc;
+        } else {
+#pragma unroll
+            for (int c = 0; c < kCols; ++c) sdst[c] = (uint8_t)(sc >> (8 * c));
+        }
+    }
+}
+
 // ------------------------------- launchers ---------------------------------
 
 static int codec_grid(int64_t work_items)
@@ -379,6 +462,40 @@ cudaError_t launch_mxfp8_quantize_bf16(const void* in, uint8_t* data, uint8_t* s
             x, data, scales, M, K, nblk);
     }
     return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_quantize_cols(const T* in, uint8_t* data, uint8_t* scales, int64_t M, int64_t K,
+                                        cudaStream_t stream)
+{
+    if (M == 0 || K == 0) return cudaSuccess;
+    const int64_t nblocks = (M + 31) / 32;
+    const uintptr_t ia = reinterpret_cast<uintptr_t>(in), da = reinterpret_cast<uintptr_t>(data),
+                    sa = reinterpret_cast<uintptr_t>(scales);
+    const bool vec = K % 4 == 0 && ia % (4 * sizeof(T)) == 0 && da % 4 == 0 && sa % 4 == 0;
+    const int64_t ngroups = vec ? K / 4 : K;
+    int64_t blocks = (ngroups * nblocks + kColsThreads - 1) / kColsThreads;
+    const int64_t cap = (int64_t)device_sm_count() * 32;
+    if (blocks > cap) blocks = cap;
+    if (vec)
+        mxfp8_quantize_cols_kernel<T, 4><<<(int)blocks, kColsThreads, 0, stream>>>(in, data, scales, M, K, ngroups,
+                                                                                  nblocks);
+    else
+        mxfp8_quantize_cols_kernel<T, 1><<<(int)blocks, kColsThreads, 0, stream>>>(in, data, scales, M, K, ngroups,
+                                                                                  nblocks);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mxfp8_quantize_cols(const float* in, uint8_t* data, uint8_t* scales, int64_t M, int64_t K,
+                                       cudaStream_t stream)
+{
+    return launch_quantize_cols<float>(in, data, scales, M, K, stream);
+}
+
+cudaError_t launch_mxfp8_quantize_bf16_cols(const void* in, uint8_t* data, uint8_t* scales, int64_t M,
+                                            int64_t K, cudaStream_t stream)
+{
+    return launch_quantize_cols<uint16_t>(static_cast<const uint16_t*>(in), data, scales, M, K, stream);
 }
 
 cudaError_t launch_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, float* out,

@@ -24,6 +24,12 @@ cudaError_t launch_mxfp8_quantize_bf16(const void* in, uint8_t* data, uint8_t* s
 cudaError_t launch_mxfp8_dequantize_bf16(const uint8_t* data, const uint8_t* scales, void* out,
                                          int64_t M, int64_t K, int64_t ld_out, cudaStream_t stream,
                                          uint32_t* zero_words = nullptr, int n_zero = 0);
+// float / BF16 [M][K] -> MXFP8 with blocks of 32 rows in each column: codes [M][K],
+// scales [ceil(M/32)][K].
+cudaError_t launch_mxfp8_quantize_cols(const float* in, uint8_t* data, uint8_t* scales, int64_t M, int64_t K,
+                                       cudaStream_t stream);
+cudaError_t launch_mxfp8_quantize_bf16_cols(const void* in, uint8_t* data, uint8_t* scales, int64_t M,
+                                            int64_t K, cudaStream_t stream);
 // D = MXFP8(dequant(C)) along N (C may be null: D = MXFP8(0)).  The K == 0 GEMM.
 cudaError_t launch_mxfp8_requantize(const uint8_t* c_data, const uint8_t* c_scales, uint8_t* d_data,
                                     uint8_t* d_scales, int64_t M, int64_t N, cudaStream_t stream);

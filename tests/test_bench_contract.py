@@ -49,3 +49,43 @@ def test_reference_arm_other_ranks_print_nothing():
     out = _run_bench("--impl", "reference", "--steps", "1",
                      env_extra={"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert out.strip() == ""
+
+
+def test_reference_line_names_its_sample_and_the_gpu_arms_config():
+    """The reference arm's step is one timed row sample: the line says so
+    (extrapolated, sample rows and seconds, ms_per_step = the sample's time, so that
+    steps x ms_per_step is the time the arm spent), and its config is the GPU arm's."""
+    import argparse
+
+    sys.path.insert(0, ROOT)
+    import bench
+
+    line = json.loads(_run_bench("--impl", "reference", "--steps", "2", "--warmup", "1").strip())
+    assert line["extrapolated"] is True and line["sample_rows"] >= 1 and line["sample_s"] > 0
+    assert abs(line["ms_per_step"] - 1e3 * line["sample_s"]) < 1.0
+    assert line["full_step_ms_extrapolated"] > line["ms_per_step"]
+    want = bench.workload_config(argparse.Namespace(workload="dense_projection", scaling="strong"), 1)
+    assert line["config"] == want
+
+
+@pytest.mark.parametrize("workload,world,rows,cols", [
+    ("dense_projection", 8, 512, 12288), ("dense_projection", 4, 1024, 12288), ("tall_skinny", 8, 16384, 2048),
+    ("wide", 8, 2048, 3584), ("square", 8, 2048, 16384), ("dense_projection", 1, 4096, 12288)])
+def test_strong_scaling_slabs(workload, world, rows, cols):
+    """Strong scaling cuts the workload's global GEMM: M-row slabs, or 32-column
+    multiples of N for the wide shape; every rank's slab has the same size."""
+    import argparse
+
+    sys.path.insert(0, ROOT)
+    import bench
+
+    a = argparse.Namespace(workload=workload, scaling="strong")
+    M, N, K, _, _ = bench.WORKLOADS[workload]
+    for r in range(world):
+        rr, cc, kk, mt, nt, shards, mode, _ = bench.layout(a, world, r)
+        assert (rr, cc, kk, mt, nt) == (rows, cols, K, M, N)
+        assert cc % 32 == 0
+    cfg = bench.workload_config(a, world)
+    assert cfg["M_per_gpu"] == rows and cfg["N_per_gpu"] == cols and cfg["M_total"] == M
+    weak = bench.layout(argparse.Namespace(workload=workload, scaling="weak"), world, world - 1)
+    assert weak[:5] == (M, N, K, M * world, N)

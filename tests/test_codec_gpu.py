@@ -239,3 +239,80 @@ def test_quantize_bf16_bit_exact(mpk_lib, cuda, kind, M, K, offset):
     d, s = _gpu_quantize_bf16(mpk_lib, bits, offset)
     wd, ws = O.quantize(O.bf16_bits_to_float(bits))
     assert np.array_equal(d, wd) and np.array_equal(s, ws)
+
+
+# ------------------------- quantize along the rows -------------------------
+
+def _cols_expected(xf):
+    """The row quantizer of the oracle on the transposed tensor, transposed back:
+    codes [M][K], scales [ceil(M/32)][K]."""
+    dT, sT = O.quantize(np.ascontiguousarray(xf.T))
+    return np.ascontiguousarray(dT.T), np.ascontiguousarray(sT.T)
+
+
+def _gpu_quantize_cols(mpk, x, offset=0):
+    """x: float32 array or bf16 bit patterns (uint16); offset in elements from an
+    aligned allocation, to exercise the general path."""
+    import torch
+
+    M, K = x.shape
+    flat = to_dev(np.ascontiguousarray(x).reshape(-1))
+    big = torch.empty(flat.numel() + offset, dtype=flat.dtype, device="cuda")
+    big[offset:].copy_(flat)
+    d = torch.full((M, K), 0xEE, dtype=torch.uint8, device="cuda")
+    s = torch.full(((M + 31) // 32, K), 0xEE, dtype=torch.uint8, device="cuda")
+    fn = mpk.mxfp8_quantize_cols_gpu if x.dtype == np.float32 else mpk.mxfp8_quantize_bf16_cols_gpu
+    fn(big.data_ptr() + offset * big.element_size(), d, s, M, K)
+    torch.cuda.synchronize()
+    return to_host(d), to_host(s)
+
+
+@pytest.mark.parametrize("kind", ["normal", "wide", "bits", "special"])
+@pytest.mark.parametrize("M,K,offset", [(256, 1024, 0), (100, 37, 0), (33, 4096, 0), (1, 5, 0), (131, 260, 1),
+                                        (64, 96, 3), (4096, 512, 0)])
+def test_quantize_cols_bit_exact(mpk_lib, cuda, kind, M, K, offset):
+    """Blocks of 32 rows per column: ragged M (a partial last block), K not a
+    multiple of 4 or an unaligned input (the one-column-per-thread path), NaN,
+    infinities and the saturation range."""
+    rng = np.random.default_rng(M * 7 + K)
+    if kind == "normal":
+        x = (rng.standard_normal((M, K)) * 0.02).astype(np.float32)
+    elif kind == "wide":
+        x = (rng.standard_normal((M, K)) * np.exp(rng.uniform(-60, 60, (M, K)))).astype(np.float32)
+    elif kind == "bits":
+        x = rng.integers(0, 1 << 32, (M, K), dtype=np.uint64).astype(np.uint32).view(np.float32)
+    else:
+        pool = np.array([0.0, -0.0, np.nan, np.inf, -np.inf, 448, 449, 464, 1e-40, 3e38, -5.0], np.float32)
+        x = rng.choice(pool, (M, K))
+    d, s = _gpu_quantize_cols(mpk_lib, x, offset)
+    wd, ws = _cols_expected(x)
+    assert np.array_equal(d, wd) and np.array_equal(s, ws)
+
+
+@pytest.mark.parametrize("M,K,offset", [(256, 2048, 0), (100, 37, 0), (65, 260, 1)])
+def test_quantize_bf16_cols_bit_exact(mpk_lib, cuda, M, K, offset):
+    """BF16 source: the column quantizer of each value widened exactly to FP32."""
+    rng = np.random.default_rng(M + K)
+    normal = O.to_bf16_bits((rng.standard_normal((M, K)) * 0.02).astype(np.float32))
+    any_bits = rng.integers(0, 1 << 16, (M, K), dtype=np.uint32).astype(np.uint16)
+    bits = np.where(rng.random((M, K)) < 0.5, normal, any_bits).astype(np.uint16)
+    d, s = _gpu_quantize_cols(mpk_lib, bits, offset)
+    wd, ws = _cols_expected(O.bf16_bits_to_float(bits))
+    assert np.array_equal(d, wd) and np.array_equal(s, ws)
+
+
+def test_quantize_cols_large_matches_row_quantizer_of_transpose(mpk_lib, cuda):
+    """16384 x 2048 N(0, 0.02^2): the column quantizer equals the library's own row
+    quantizer applied to the transposed tensor on the device, bit for bit."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn((16384, 2048), generator=g, device="cuda") * 0.02
+    d, s = mpk_lib.quantize_cols(x)
+    dT, sT = mpk_lib.quantize(x.t().contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(d, dT.t()) and torch.equal(s, sT.t())
+    d16, s16 = mpk_lib.quantize_cols(x.to(torch.bfloat16))
+    dT16, sT16 = mpk_lib.quantize(x.to(torch.bfloat16).float().t().contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(d16, dT16.t()) and torch.equal(s16, sT16.t())

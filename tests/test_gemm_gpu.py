@@ -377,6 +377,7 @@ def _sample_rows(M):
     (4096, 4096, 11008, 44, 0.02),     # long K (344 MX blocks per row)
     (131072, 2048, 2048, 45, 0.02),    # tall-skinny
     (2048, 28672, 8192, 46, 0.02),     # wide
+    (16384, 16384, 16384, 46, 0.02),   # square
     (4096, 4096, 4096, 44, 0.01),      # dynamic-range sweep
     (4096, 4096, 4096, 44, 0.1),
     (4096, 4096, 4096, 44, 1.0),
@@ -415,3 +416,22 @@ def test_full_size_row_sampled(mpk_lib, cuda, M, N, K, seed, std):
                  ref_pass_mark=False)
     del Ad, As, B, Cd, Cs, D, Ds
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("M,N,K,seed", [(4096, 12288, 4096, 43), (131072, 2048, 2048, 45)])
+def test_config_input_streams_row_sampled(mpk_lib, cuda, M, N, K, seed):
+    """The dense projection and tall-skinny configurations on their own inputs:
+    N(0, 0.02^2) drawn by one mt19937(seed) engine and one normal_distribution<float>,
+    A then B then C (tests/test_gemm_correctness.cu:23-30 of the reference), A and C
+    quantized by the host quantizer, B rounded to BF16 -- byte-identical to the
+    reference's recipe.  D on the GPU against the exact FP32 gold on sampled rows,
+    and against the reference's own FP8-TC kernel on the same device inputs."""
+    inp = O.make_gemm_inputs(M, N, K, seed=seed)
+    Dd, Ds = run_gemm(mpk_lib, inp)
+    rows = _sample_rows(M)
+    k7 = None
+    if have_ref:
+        d7, s7 = run_ref_k7(inp)
+        k7 = (d7[rows], s7[rows])
+    check_parity(Dd[rows], Ds[rows], O.gold_mx(inp, rows=rows), f"{M}x{N}x{K} mt19937({seed})", k7,
+                 ref_pass_mark=False)

@@ -27,7 +27,14 @@ def _schedule(mpk, mode):
     return _Ctx()
 
 
-def _against_tiles(mpk, inp, label, with_c=True):
+def _sample_rows(M):
+    rows = {0, 1, 127, 128, 255, 256, M // 2, M - 129, M - 128, M - 1}
+    rng = np.random.default_rng(M)
+    rows |= set(int(r) for r in rng.integers(0, M, 54))
+    return np.array(sorted(r for r in rows if 0 <= r < M), np.int64)
+
+
+def _against_tiles(mpk, inp, label, with_c=True, rows=None):
     d0, s0 = run_gemm(mpk, inp, with_c=with_c)
     d0b, s0b = run_gemm(mpk, inp, with_c=with_c)
     assert np.array_equal(d0, d0b) and np.array_equal(s0, s0b), "second call differs"
@@ -36,18 +43,24 @@ def _against_tiles(mpk, inp, label, with_c=True):
     hist = O.mx_ulp_hist(d0, s0, dt, st)
     print(f"{label}: vs whole tiles {hist}")
     assert hist[2] == 0 and hist[3] == 0
-    check_parity(d0, s0, O.gold_mx(inp), label)
+    if rows is None:
+        check_parity(d0, s0, O.gold_mx(inp), label)
+    else:  # exact gold for a sample of rows (row i of D depends on rows i of A and C only)
+        check_parity(d0[rows], s0[rows], O.gold_mx(inp, rows=rows), label, ref_pass_mark=False)
     assert mpk.device_status() == 0
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 4096, 4096), (256, 1024, 4096), (512, 1536, 2048),
-                                   (1024, 768, 2048), (300, 520, 1112), (129, 520, 1104)])
+@pytest.mark.parametrize("M,N,K", [(1024, 5632, 640), (1024, 12288, 1024), (512, 12288, 4096),
+                                   (1024, 12288, 4096), (2048, 3584, 8192)])
 def test_default_schedule_split_wave(mpk_lib, cuda, M, N, K):
-    """Shapes whose default plan spreads tiles over the SM pairs."""
+    """Shapes whose default plan spreads the last wave's tiles over the SM pairs,
+    among them the per-GPU slabs of the dense projection on 8 and 4 GPUs and of the
+    wide shape on 8 GPUs."""
     tiles, sk_tiles, pairs = mpk_lib.gemm_plan(M, N, K)
     assert sk_tiles > 0 and pairs > sk_tiles, (tiles, sk_tiles, pairs)
     inp = O.make_gemm_inputs(M, N, K, seed=M + N + K)
-    _against_tiles(mpk_lib, inp, f"stream-K {M}x{N}x{K} ({sk_tiles} tiles on {pairs} pairs)")
+    rows = _sample_rows(M) if M * N * K > 4e9 else None
+    _against_tiles(mpk_lib, inp, f"stream-K {M}x{N}x{K} ({sk_tiles} tiles on {pairs} pairs)", rows=rows)
 
 
 @pytest.mark.parametrize("M,N,K", [(256, 256, 2048), (1, 8, 16), (65, 7, 17), (200, 264, 80),
@@ -91,11 +104,19 @@ def test_forced_stream_k_exotic_scales_and_nan(mpk_lib, cuda):
     assert O.mx_ulp_hist(d0, s0, dt, st)[3] == 0
 
 
-def test_graph_replay_resets_the_hand_off(mpk_lib, cuda):
+@pytest.fixture
+def forced_stream_k(mpk_lib):
+    prev = mpk_lib.set_gemm_schedule(mpk_lib.SCHEDULE_STREAM_K)
+    yield mpk_lib
+    mpk_lib.set_gemm_schedule(prev)
+
+
+def test_graph_replay_resets_the_hand_off(forced_stream_k, cuda):
     """A captured call replays with fresh counters each time (the captured pre-pass
     zeroes them), giving the eager call's D bit for bit."""
     import torch
 
+    mpk_lib = forced_stream_k
     M, N, K = 512, 1024, 4096
     assert mpk_lib.gemm_plan(M, N, K)[1] > 0
     inp = O.make_gemm_inputs(M, N, K, seed=77)
@@ -119,7 +140,7 @@ def test_graph_replay_resets_the_hand_off(mpk_lib, cuda):
     assert mpk_lib.device_status() == 0
 
 
-def test_concurrent_streams_and_threads(mpk_lib, cuda):
+def test_concurrent_streams_and_threads(forced_stream_k, cuda):
     """Stream-K calls in flight on several streams at once from several host
     threads: the pairs of one call may not all be resident while another call
     runs, and a pair waits only for pairs that started before it, so every call
@@ -128,6 +149,7 @@ def test_concurrent_streams_and_threads(mpk_lib, cuda):
 
     import torch
 
+    mpk_lib = forced_stream_k
     shapes = [(512, 1024, 4096), (256, 2048, 2048), (1024, 768, 2048), (128, 4096, 4096)]
     cases = []
     for i, (M, N, K) in enumerate(shapes):
@@ -161,11 +183,12 @@ def test_concurrent_streams_and_threads(mpk_lib, cuda):
     assert mpk_lib.device_status() == 0
 
 
-def test_small_workspace_falls_back_to_whole_tiles(mpk_lib, cuda):
+def test_small_workspace_falls_back_to_whole_tiles(forced_stream_k, cuda):
     """A caller workspace with room for the operands but not for the partials runs
     whole tiles: D equals the whole-tile schedule's bit for bit."""
     import torch
 
+    mpk_lib = forced_stream_k
     M, N, K = 256, 1024, 4096
     assert mpk_lib.gemm_plan(M, N, K)[1] > 0
     inp = O.make_gemm_inputs(M, N, K, seed=9)
