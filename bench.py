@@ -626,7 +626,7 @@ def run_gemm_arm(args, world, rank, local, dist):
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
-        "higher_is_better": True, "scaling": args.scaling if world > 1 else "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (N(0,0.02^2) drawn on device, torch Philox seeded; A/C quantized to "
                 "MXFP8 by the library, B rounded to BF16)",
@@ -989,7 +989,7 @@ def run_reference_arm(args, world, rank):
     return {
         "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(statistics.mean(secs) * 1e3, 3),
-        "higher_is_better": True, "scaling": args.scaling if world > 1 else "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
         "dtype": "f32", "data": "synthetic N(0,0.02^2)", "impl": "reference",
         "config": workload_config(args, world),
         "step": f"one timed sample of {sample_rows} rows of the {M}x{N}x{K} workload on {cb.threads} host threads",

@@ -22,10 +22,16 @@
 
 // Same signature and argument meaning as the reference (include/gemm_kernels.h:12-16),
 // any M, N, K.  Differences: no per-call cudaMalloc/cudaFree or implicit device
-// synchronization (the A workspace comes from a pooled, stream-ordered reserve); any
-// failure (no sm_100 device, out of memory, a shape the on-chip kernel cannot take
-// while the stream is being captured) prints a message and exits, as the
-// reference's CUDA_CHECK does.
+// synchronization.  The workspace (A's BF16 copy, M*K*2 bytes, plus the stream-K
+// partials when the schedule uses them, mpk_gemm_workspace_size) comes from a
+// library-owned stream-ordered pool that keeps what it has reserved: the first call
+// of each larger workspace size on a device grows the pool (the driver maps new
+// device memory inside that call); calls of that size or smaller afterwards reuse
+// it without any driver allocation, until mpk_release_workspace_pool.  A caller
+// that must know its footprint before its first request makes one call of its
+// largest size at set-up.  Any failure (no sm_100 device, out of memory, a shape the
+// on-chip kernel cannot take while the stream is being captured) prints a message
+// and exits, as the reference's CUDA_CHECK does.
 inline void gemm_fp8_tensorcore(const uint8_t* d_A_data, const uint8_t* d_A_scales,
                                 const __nv_bfloat16* d_B, const uint8_t* d_C_data,
                                 const uint8_t* d_C_scales, uint8_t* d_D_data, uint8_t* d_D_scales,
@@ -34,7 +40,7 @@ inline void gemm_fp8_tensorcore(const uint8_t* d_A_data, const uint8_t* d_A_scal
     const int st = mpk_gemm_mxfp8_bf16(d_A_data, d_A_scales, d_B, d_C_data, d_C_scales, d_D_data,
                                        d_D_scales, M, N, K, stream);
     if (st != MPK_SUCCESS) {
-        fprintf(stderr, "gemm_fp8_tensorcore failed: %s (%s)\n", mpk_status_string(st), mpk_last_error());
+        fprintf(stderr, "gemm_fp8_tensorcore failed: %s (%s)\n", mpk_status_string(st), mpk_last_error_string());
         exit(EXIT_FAILURE);
     }
 }

@@ -17,7 +17,7 @@
  *
  * Differences from the reference, by design:
  *   - every entry point returns a status code (0 = success) instead of calling
- *     exit() on failure; a detail message is available from mpk_last_error();
+ *     exit() on failure; a detail message is available from mpk_last_error_string();
  *   - no call synchronizes the device; every launch is stream-ordered;
  *   - mpk_gemm_mxfp8_bf16 does not cudaMalloc/cudaFree per call: the workspace of
  *     its A pre-pass (about M*K*2 bytes, mpk_gemm_workspace_size) comes from a

@@ -78,7 +78,7 @@ namespace mpk_compat {
 inline void check(int status, const char* what)
 {
     if (status != MPK_SUCCESS) {
-        fprintf(stderr, "%s failed: %s (%s)\n", what, mpk_status_string(status), mpk_last_error());
+        fprintf(stderr, "%s failed: %s (%s)\n", what, mpk_status_string(status), mpk_last_error_string());
         exit(EXIT_FAILURE);
     }
 }

@@ -323,36 +323,93 @@ __device__ __forceinline__ bool sk_wait_partials(const Params& p, int c_first, i
     return true;
 }
 
-// Owner side: add the contributors' partial sums (clusters c_first..c_last, in a
-// fixed order: the highest K range first after this CTA's own) into this CTA's
-// accumulator in tensor memory, chunk by chunk, before the ordinary epilogue reads
-// it.  `tacc` is this warp's lane quarter of the accumulator; warp-collective.
-__device__ __noinline__ void sk_merge_partials(const Params& p, uint32_t tacc, int c_first, int c_last,
-                                               uint32_t rank, int r, bool row_ok, int nchunks)
+// Owner side.  The contributors' partials reach the owner through a staging area
+// of `slots` pieces of 16 KiB in shared memory (one contributor's 32 columns x
+// 128 rows, contiguous in its partial): piece i = 32-column chunk i / n of
+// contributor c_last - i % n (n contributors, highest K range first) goes to slot
+// i % slots.  Warp 2 (idle otherwise) waits for the contributors' arrivals, then
+// streams the pieces in by bulk copies, refilling a slot once all 128 epilogue
+// threads have read it; it starts as soon as the partials are there, so the first
+// pieces are usually in shared memory before the owner's own accumulator is done.
+// The epilogue adds them chunk by chunk while it finishes the tile.  Reading the
+// partials through bulk copies keeps `slots` x 16 KiB in flight without spending
+// registers, which is what the merge needs: it is bound by the latency of L2.
+constexpr uint32_t kSkPieceBytes = BM * 32 * 4;
+
+struct MergeStage {
+    const uint8_t* stage;      // slots x kSkPieceBytes of shared memory
+    int slots;
+    uint32_t pfull0, pempty0;  // slots' full (1 arrival + bytes) and empty (128 arrivals) barriers
+    volatile int* never_abort;
+};
+
+// Warp 2, one lane: the bulk copies of this cluster's owner unit's partials (if
+// the cluster has an owner unit and this CTA has rows of it).
+__device__ __noinline__ void sk_issue_merge(const Params& p, int cluster, int nclusters, uint32_t rank,
+                                            const MergeStage ms, volatile int* abort_flag)
 {
-#pragma unroll 1
-    for (int chunk = 0; chunk < nchunks; ++chunk) {
-        uint32_t raw[32];
-        tmem_ld_32x32b_x32(tacc + 32u * chunk, raw);
-        tmem_ld_wait();
+    UnitWalk walk(p, cluster, nclusters);
+    Unit u;
+    bool found = false;
+    while (walk.hi > walk.lo && walk.next(p, u))
+        if (u.kind == kUnitOwner) {
+            found = true;
+            break;
+        }
+    if (!found || (int64_t)u.m0 + BM * (int)rank >= p.M) return;
+    const int c_first = u.first_contrib, c_last = cluster - 1, n = c_last - c_first + 1;
+    const int nchunks = min(BN / 32, (p.N - u.n0 + 31) / 32);
+    if (!sk_wait_partials(p, c_first, c_last, rank, abort_flag)) return;
+    fence_proxy_async_global();  // the bulk copies read what the acquires made visible
+    const uint32_t stage_s = smem_u32(ms.stage);
+    const int npieces = n * nchunks;
+    int issued = 0;
+    bool ok = true;
+    for (int i = 0; i < npieces; ++i) {
+        const int slot = i % ms.slots;
+        if (i >= ms.slots) {  // the slot's previous piece must have been read by every thread
+            ok = mbar_wait(ms.pempty0 + 8u * slot, (uint32_t)(i / ms.slots - 1) & 1u, abort_flag, p.status,
+                           kSitePartials, p.timeout_ns);
+            if (!ok) break;
+        }
+        const float4* src = sk_slot(p, c_last - i % n, rank) + (size_t)(i / n) * 8 * BM;
+        mbar_arrive_expect_tx(ms.pfull0 + 8u * slot, kSkPieceBytes);
+        bulk_load_g2s(stage_s + (uint32_t)slot * kSkPieceBytes, src, kSkPieceBytes, ms.pfull0 + 8u * slot);
+        ++issued;
+    }
+    if (!ok) {
+        // Copies in flight land before shared memory can be released.
+        for (int i = issued > ms.slots ? issued - ms.slots : 0; i < issued; ++i)
+            mbar_wait(ms.pfull0 + 8u * (i % ms.slots), (uint32_t)(i / ms.slots) & 1u, ms.never_abort, nullptr, 0,
+                      kDrainTimeoutNs);
+    }
+}
+
+// Epilogue side: add the n pieces of 32-column chunk `chunk` to this thread's row
+// (v), releasing their slots.  Returns false if a bounded wait gave up.
+__device__ __forceinline__ bool sk_add_pieces(const Params& p, const MergeStage& ms, int n, int chunk, int r,
+                                              bool row_ok, float (&v)[32], volatile int* abort_flag)
+{
+    for (int j = 0; j < n; ++j) {
+        const int i = chunk * n + j;
+        const int slot = i % ms.slots;
+        if (!mbar_wait(ms.pfull0 + 8u * slot, (uint32_t)(i / ms.slots) & 1u, abort_flag, p.status, kSitePartials,
+                       p.timeout_ns))
+            return false;
         if (row_ok) {
-            for (int c = c_last; c >= c_first; --c) {
-                const float4* src = sk_slot(p, c, rank) + (size_t)chunk * 8 * BM + r;
-                float4 x[8];
+            const float4* x = reinterpret_cast<const float4*>(ms.stage + (size_t)slot * kSkPieceBytes) + r;
 #pragma unroll
-                for (int q = 0; q < 8; ++q) x[q] = __ldcg(src + q * BM);
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    raw[4 * q + 0] = __float_as_uint(__uint_as_float(raw[4 * q + 0]) + x[q].x);
-                    raw[4 * q + 1] = __float_as_uint(__uint_as_float(raw[4 * q + 1]) + x[q].y);
-                    raw[4 * q + 2] = __float_as_uint(__uint_as_float(raw[4 * q + 2]) + x[q].z);
-                    raw[4 * q + 3] = __float_as_uint(__uint_as_float(raw[4 * q + 3]) + x[q].w);
-                }
+            for (int q = 0; q < 8; ++q) {
+                const float4 y = x[q * BM];
+                v[4 * q + 0] += y.x;
+                v[4 * q + 1] += y.y;
+                v[4 * q + 2] += y.z;
+                v[4 * q + 3] += y.w;
             }
         }
-        tmem_st_32x32b_x32(tacc + 32u * chunk, raw);
+        mbar_arrive(ms.pempty0 + 8u * slot);
     }
-    tmem_st_wait();
+    return true;
 }
 
 // Contributor side: store this CTA's accumulator (this warp's lane quarter `tacc`)
@@ -360,16 +417,22 @@ __device__ __noinline__ void sk_merge_partials(const Params& p, uint32_t tacc, i
 __device__ __noinline__ void sk_store_partial(float4* slot_row, uint32_t tacc, bool row_ok, int nchunks)
 {
 #pragma unroll 1
-    for (int c = 0; c < nchunks; ++c) {
-        uint32_t raw[32];
-        tmem_ld_32x32b_x32(tacc + 32u * c, raw);
+    for (int c = 0; c < nchunks; c += 2) {  // two chunks per tensor-memory wait
+        const bool two = c + 1 < nchunks;
+        uint32_t raw[2][32];
+        tmem_ld_32x32b_x32(tacc + 32u * c, raw[0]);
+        if (two) tmem_ld_32x32b_x32(tacc + 32u * (c + 1), raw[1]);
         tmem_ld_wait();
         if (row_ok) {
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-                __stcg(slot_row + (size_t)(c * 8 + q) * BM,
-                       make_float4(__uint_as_float(raw[4 * q]), __uint_as_float(raw[4 * q + 1]),
-                                   __uint_as_float(raw[4 * q + 2]), __uint_as_float(raw[4 * q + 3])));
+            for (int h = 0; h < 2; ++h) {
+                if (h == 1 && !two) break;
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    __stcg(slot_row + (size_t)((c + h) * 8 + q) * BM,
+                           make_float4(__uint_as_float(raw[h][4 * q]), __uint_as_float(raw[h][4 * q + 1]),
+                                       __uint_as_float(raw[h][4 * q + 2]), __uint_as_float(raw[h][4 * q + 3])));
+            }
         }
     }
 }
@@ -517,17 +580,26 @@ __device__ __forceinline__ uint32_t quantize_block32(float (&v)[32], uint4& c0, 
 // from TMEM itself (warp-collective; every lane calls this together), element-wise
 // C loads and D stores, columns past N kept out of the block amax.  Out of line to
 // keep the epilogue's hot code small.
+// A stream-K owner's chunk (n_merge > 0) also adds its contributors' pieces; returns
+// false if that gave up waiting (the warp then leaves the tile together).
 template <bool kGather>
-__device__ __noinline__ void epilogue_ragged_chunk(const Params& p, uint32_t taddr, uint32_t cscale,
+__device__ __noinline__ bool epilogue_ragged_chunk(const Params& p, uint32_t taddr, uint32_t cscale,
                                                    bool has_c, bool row_ok, int64_t grow, int col0,
-                                                   int valid)
+                                                   int valid, const MergeStage* ms, int n_merge, int chunk,
+                                                   int r, volatile int* abort_flag)
 {
     uint32_t raw[32];
     tmem_ld_32x32b_x32(taddr, raw);
     tmem_ld_wait();
     float v[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = (i < valid) ? __uint_as_float(raw[i]) : 0.0f;
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]);
+    if (n_merge > 0) {
+        const bool ok = sk_add_pieces(p, *ms, n_merge, chunk, r, row_ok, v, abort_flag);
+        if (!__all_sync(0xFFFFFFFFu, ok)) return false;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = (i < valid) ? v[i] : 0.0f;
     if (has_c && row_ok) {
         const float sc = e8m0_to_f32(cscale);
 #pragma unroll
@@ -546,6 +618,7 @@ __device__ __noinline__ void epilogue_ragged_chunk(const Params& p, uint32_t tad
             if (i < valid) p.D_data[doff + i] = (uint8_t)(dw[i >> 2] >> (8 * (i & 3)));
         p.D_scales[soff] = (uint8_t)sd;
     }
+    return true;
 }
 
 // One full 32-column D chunk (two 16-byte stores) and its scale byte, into this
@@ -635,11 +708,12 @@ __device__ __forceinline__ void forward_tile(const Params& p, int64_t r0, int nr
 //   stream-K contributor: store the FP32 accumulator as this CTA's partial and count
 //     this thread's arrival;
 // and release the accumulator on rank 0's tempty barrier.
-template <bool kGather>
+template <bool kGather, bool kStreamK>
 __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base, uint32_t tfull0,
                                          uint32_t tempty_base, int cluster, int nclusters,
                                          uint32_t rank, int warp, int lane, volatile int* abort_flag,
-                                         uint32_t epi_done = 0u, volatile int* tiles_done = nullptr)
+                                         uint32_t epi_done = 0u, volatile int* tiles_done = nullptr,
+                                         MergeStage ms = MergeStage{nullptr, 0, 0u, 0u, nullptr})
 {
     auto tfull = [&](int a) { return tfull0 + 8u * a; };
     const int quad = warp & 3;                 // TMEM lanes this warp may access
@@ -657,8 +731,8 @@ __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base
         const int64_t grow = (int64_t)m0 + BM * (int)rank + r;
         const bool row_ok = grow < p.M;
         const int nchunks = min(bn / 32, (p.N - n0 + 31) / 32);
-        const uint32_t tacc = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-        if (u.kind == kUnitContrib) {
+        if (kStreamK && u.kind == kUnitContrib) {
+            const uint32_t tacc = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
             if (!mbar_wait(tfull(acc), acc_ph, abort_flag, p.status, kSiteTmemFull, p.timeout_ns)) break;
             tc_fence_after();
             sk_store_partial(sk_slot(p, cluster, rank) + r, tacc, row_ok, nchunks);
@@ -668,6 +742,11 @@ __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base
             red_release_gpu_add(p.sk_sync + 1 + 2 * cluster + (int)rank, 1u);
             continue;
         }
+        // Stream-K owner: the tile's other K ranges are the partials of n_merge
+        // clusters (first_contrib .. cluster-1), added chunk by chunk below (none when
+        // this CTA has no rows of the tile: its issuer copies nothing).
+        const int n_merge = kStreamK && u.kind == kUnitOwner && (int64_t)m0 + BM * (int)rank < p.M
+                                ? cluster - u.first_contrib : 0;
         bool full_seen = false;
 #pragma unroll
         for (int c0 = 0; c0 < BN / 32; c0 += kCPrefetch) {
@@ -698,14 +777,6 @@ __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base
                 }
                 tc_fence_after();
                 full_seen = true;
-                if (u.kind == kUnitOwner) {
-                    // The tile's other K ranges: partials of clusters first_contrib .. cluster-1.
-                    if (!sk_wait_partials(p, u.first_contrib, cluster - 1, rank, abort_flag)) {
-                        aborted = true;
-                        break;
-                    }
-                    sk_merge_partials(p, tacc, u.first_contrib, cluster - 1, rank, r, row_ok, nchunks);
-                }
             }
 #pragma unroll
             for (int ci = 0; ci < kCPrefetch; ++ci) {
@@ -721,6 +792,13 @@ __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base
                     float v[32];
 #pragma unroll
                     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]);
+                    if (kStreamK && n_merge > 0) {
+                        const bool ok = sk_add_pieces(p, ms, n_merge, c, r, row_ok, v, abort_flag);
+                        if (!__all_sync(0xFFFFFFFFu, ok)) {  // the warp leaves together
+                            aborted = true;
+                            break;
+                        }
+                    }
                     if (has_c) {
                         const float sc = e8m0_to_f32(cs[ci]);
                         const uint32_t cw[8] = {cq[ci][0].x, cq[ci][0].y, cq[ci][0].z, cq[ci][0].w,
@@ -738,10 +816,13 @@ __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base
                     uint4 d0, d1;
                     const uint32_t sd = quantize_block32(v, d0, d1);
                     if (row_ok) store_d_chunk<kGather>(p, grow, col0, d0, d1, sd);
-                } else {
-                    epilogue_ragged_chunk<kGather>(p, taddr, cs[ci], has_c, row_ok, grow, col0, valid);
+                } else if (!epilogue_ragged_chunk<kGather>(p, taddr, cs[ci], has_c, row_ok, grow, col0, valid,
+                                                           &ms, n_merge, c, r, abort_flag)) {
+                    aborted = true;
+                    break;
                 }
             }
+            if (aborted) break;
         }
         if (aborted) break;
         // An item with no columns inside N (the second half of a split tile at the
@@ -1037,8 +1118,8 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
     } else {
         setmaxnreg_inc<kEpiRegs>();
         // -------------------------------- epilogue --------------------------------
-        run_epilogue<false>(p, tmem_base, tfull(0), mapa_shared(tempty(0), 0), cluster, nclusters, rank, warp,
-                     lane, abort_flag);
+        run_epilogue<false, false>(p, tmem_base, tfull(0), mapa_shared(tempty(0), 0), cluster, nclusters, rank,
+                                   warp, lane, abort_flag);
     }
 
     // ------------------------------- teardown -------------------------------------
@@ -1068,46 +1149,63 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
 // B half (16 KiB), both completing on rank 0's full barrier.
 //
 // Warps: 0 TMA producer, 1 TMEM owner + MMA issuer (rank 0), 2-3 copy warps of the
-// fused all-gather (idle otherwise), 4-7 epilogue.  Launched after the A pre-pass with
-// programmatic stream serialization: only the producer waits for the pre-pass.
+// fused all-gather (otherwise warp 2 streams a stream-K owner's partials in), 4-7
+// epilogue.  Launched after the A pre-pass with programmatic stream serialization:
+// only the producer waits for the pre-pass.
+//
+// Shared memory: kStages ring stages, then kSlots 16 KiB stream-K staging pieces.
+// Three variants: whole tiles (7 stages), stream-K (5 stages + 4 pieces: the
+// merge's staging costs two stages, which the mainloop does not need at full speed)
+// and the fused all-gather (7 stages, whole tiles).
 // ============================================================================
-#ifndef MPK_P_STAGES
-#define MPK_P_STAGES 7
-#endif
-constexpr int P_STAGES = MPK_P_STAGES;
 constexpr int P_THREADS = 256;
 constexpr int P_FIRST_EPI_WARP = 4;
-constexpr int P_OFF_B = 0;
-constexpr int P_OFF_A = P_OFF_B + P_STAGES * B_BYTES;
-constexpr int P_OFF_BAR = P_OFF_A + P_STAGES * A16_BYTES;
-// barriers: full[S], empty[S], tfull[2], tempty[2], drain, epi_done
-constexpr int P_NUM_BARS = 2 * P_STAGES + 6;
-constexpr int P_OFF_MISC = P_OFF_BAR + P_NUM_BARS * 8;
-// misc: TMEM address, abort flag, teardown flag, units done (all-gather), cluster ticket
-constexpr int P_SMEM_BYTES = P_OFF_MISC + 32 + 1024;
-static_assert(P_SMEM_BYTES <= 232448, "exceeds the sm_100 per-block shared memory limit");
+constexpr int P_TILE_STAGES = 7;                      // whole-tile and all-gather variants
+constexpr int P_SK_STAGES = 5, P_SK_SLOTS = 4;        // stream-K variant
+
+template <int kStages, int kSlots>
+struct PLayout {
+    static constexpr int OFF_B = 0;
+    static constexpr int OFF_A = OFF_B + kStages * B_BYTES;
+    static constexpr int OFF_STAGE = OFF_A + kStages * A16_BYTES;
+    static constexpr int OFF_BAR = OFF_STAGE + kSlots * (int)kSkPieceBytes;
+    // barriers: full[S], empty[S], tfull[2], tempty[2], drain, epi_done, piece_full[P],
+    // piece_empty[P]
+    static constexpr int NUM_BARS = 2 * kStages + 6 + 2 * kSlots;
+    static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+    // misc: TMEM address, abort flag, teardown flag, units done (all-gather), cluster ticket
+    static constexpr int SMEM_BYTES = OFF_MISC + 32 + 1024;
+    static_assert(SMEM_BYTES <= 232448, "exceeds the sm_100 per-block shared memory limit");
+};
 static_assert(BK * BN == B_BYTES, "per-stage B bytes of one CTA are BK * item width");
 
-template <bool kGather>
+template <bool kGather, int kStages, int kSlots>
 __global__ void __launch_bounds__(P_THREADS, 1)
 gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
                         const __grid_constant__ CUtensorMap tmap_b, const Params p)
 {
+    using Lay = PLayout<kStages, kSlots>;
+    constexpr bool kStreamK = kSlots > 0;
+    static_assert(!(kGather && kStreamK), "the fused all-gather runs whole tiles");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t bar0 = sbase + P_OFF_BAR;
+    const uint32_t bar0 = sbase + Lay::OFF_BAR;
     auto full = [&](int s) { return bar0 + 8u * s; };
-    auto empty = [&](int s) { return bar0 + 8u * (P_STAGES + s); };
-    auto tfull = [&](int a) { return bar0 + 8u * (2 * P_STAGES + a); };
-    auto tempty = [&](int a) { return bar0 + 8u * (2 * P_STAGES + 2 + a); };
-    const uint32_t drain = bar0 + 8u * (2 * P_STAGES + 4);
-    const uint32_t epi_done = bar0 + 8u * (2 * P_STAGES + 5);  // fused all-gather only
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + P_OFF_MISC);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + P_OFF_MISC + 4);
-    volatile int* never_abort = reinterpret_cast<volatile int*>(smem + P_OFF_MISC + 8);
-    volatile int* tiles_done = reinterpret_cast<volatile int*>(smem + P_OFF_MISC + 12);
-    volatile uint32_t* ticket = reinterpret_cast<volatile uint32_t*>(smem + P_OFF_MISC + 16);
+    auto empty = [&](int s) { return bar0 + 8u * (kStages + s); };
+    auto tfull = [&](int a) { return bar0 + 8u * (2 * kStages + a); };
+    auto tempty = [&](int a) { return bar0 + 8u * (2 * kStages + 2 + a); };
+    const uint32_t drain = bar0 + 8u * (2 * kStages + 4);
+    const uint32_t epi_done = bar0 + 8u * (2 * kStages + 5);  // fused all-gather only
+    const uint32_t piece_full0 = bar0 + 8u * (2 * kStages + 6);  // stream-K only
+    const uint32_t piece_empty0 = piece_full0 + 8u * kSlots;
+    const MergeStage ms{smem + Lay::OFF_STAGE, kSlots, piece_full0, piece_empty0,
+                        reinterpret_cast<volatile int*>(smem + Lay::OFF_MISC + 8)};
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Lay::OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Lay::OFF_MISC + 4);
+    volatile int* never_abort = reinterpret_cast<volatile int*>(smem + Lay::OFF_MISC + 8);
+    volatile int* tiles_done = reinterpret_cast<volatile int*>(smem + Lay::OFF_MISC + 12);
+    volatile uint32_t* ticket = reinterpret_cast<volatile uint32_t*>(smem + Lay::OFF_MISC + 16);
     const bool forward = kGather && p.n_extra > 0;
 
     const int warp = threadIdx.x >> 5;
@@ -1117,7 +1215,7 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
     const int nclusters = (int)nclusters_x();
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < P_STAGES; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(full(s), 1);
             mbar_init(empty(s), 1);
         }
@@ -1127,6 +1225,10 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
         }
         mbar_init(drain, 1);
         mbar_init(epi_done, 4 * 32);
+        for (int i = 0; i < kSlots; ++i) {
+            mbar_init(piece_full0 + 8u * i, 1);
+            mbar_init(piece_empty0 + 8u * i, kEpilogueWarps * 32);
+        }
         *abort_flag = 0;
         *never_abort = 0;
         *tiles_done = 0;
@@ -1184,21 +1286,21 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
                     }
                     if (rank == 0) mbar_arrive_expect_tx(full(s), tx);
                     const uint32_t fb = mapa_shared(full(s), 0);
-                    tma_load_2d_pair(sbase + P_OFF_A + s * A16_BYTES, &tmap_a16, fb, kb * BK, row0);
+                    tma_load_2d_pair(sbase + Lay::OFF_A + s * A16_BYTES, &tmap_a16, fb, kb * BK, row0);
                     for (int j = 0; j < u.bn / 128; ++j)
-                        tma_load_2d_pair(sbase + P_OFF_B + s * B_BYTES + j * B_BOX_BYTES, &tmap_b, fb,
+                        tma_load_2d_pair(sbase + Lay::OFF_B + s * B_BYTES + j * B_BOX_BYTES, &tmap_b, fb,
                                          col0 + 64 * j, kb * BK);
                     ++issued;
-                    if (++s == P_STAGES) { s = 0; ph ^= 1u; }
+                    if (++s == kStages) { s = 0; ph ^= 1u; }
                 }
             }
             if (!ok) {
                 producer_aborted = true;
-                const int outstanding = issued < P_STAGES ? issued : P_STAGES;
+                const int outstanding = issued < kStages ? issued : kStages;
                 int ss = s;
                 uint32_t pp = ph;
                 for (int i = 0; i < outstanding; ++i) {
-                    if (--ss < 0) { ss = P_STAGES - 1; pp ^= 1u; }
+                    if (--ss < 0) { ss = kStages - 1; pp ^= 1u; }
                     if (rank == 0) mbar_wait(full(ss), pp, never_abort, nullptr, 0, kDrainTimeoutNs);
                 }
             }
@@ -1229,8 +1331,8 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = sbase + P_OFF_A + s * A16_BYTES;
-                    const uint32_t b_addr = sbase + P_OFF_B + s * B_BYTES;
+                    const uint32_t a_addr = sbase + Lay::OFF_A + s * A16_BYTES;
+                    const uint32_t b_addr = sbase + Lay::OFF_B + s * B_BYTES;
 #pragma unroll
                     for (int k = 0; k < BK / UMMA_K; ++k) {
                         const uint64_t adesc = umma_smem_desc_sw128(a_addr + k * UMMA_K * 2, 16, 1024);
@@ -1238,7 +1340,7 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
                         umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb != u.kb0 || k != 0) ? 1u : 0u);
                     }
                     umma_commit_pair_mc(empty(s), 0x3);
-                    if (++s == P_STAGES) { s = 0; ph ^= 1u; }
+                    if (++s == kStages) { s = 0; ph ^= 1u; }
                 }
                 if (!ok) break;
                 umma_commit_pair_mc(tfull(acc), 0x3);
@@ -1247,8 +1349,11 @@ gemm_bf16a_mxfp8_kernel(const __grid_constant__ CUtensorMap tmap_a16,
             mbar_wait(drain, 0, never_abort, nullptr, 0, kDrainTimeoutNs);
         }
     } else if (warp >= P_FIRST_EPI_WARP) {
-        run_epilogue<kGather>(p, tmem_base, tfull(0), mapa_shared(tempty(0), 0), cluster, nclusters, rank, warp,
-                              lane, abort_flag, epi_done, forward ? tiles_done : nullptr);
+        run_epilogue<kGather, kStreamK>(p, tmem_base, tfull(0), mapa_shared(tempty(0), 0), cluster, nclusters,
+                                        rank, warp, lane, abort_flag, epi_done, forward ? tiles_done : nullptr, ms);
+    } else if (kStreamK && warp == 2) {
+        // ---------- stream-K: bulk copies of the partials an owner unit adds ----------
+        if (lane == 0) sk_issue_merge(p, cluster, nclusters, rank, ms, abort_flag);
     } else if (forward) {
         // ---------------- fused all-gather: copy warps 2 and 3 ----------------
         // Forward every tile this CTA's epilogue has finished (tiles_done counts
@@ -1534,6 +1639,7 @@ int ensure_smem_attr(const void* kernel, int bytes, bool* flag)
 
 bool g_smem_attr_bf16a[64] = {};
 bool g_smem_attr_gather[64] = {};
+bool g_smem_attr_sk[64] = {};
 
 }  // namespace
 
@@ -1718,12 +1824,6 @@ int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scale
             p.Ds_extra[i] = gather->Ds_extra[i];
             if (reinterpret_cast<uintptr_t>(p.D_extra[i]) & 15u) p.vec_cd = 0;
         }
-        if ((rc = ensure_smem_attr((const void*)gemm_bf16a_mxfp8_kernel<true>, P_SMEM_BYTES,
-                                   &g_smem_attr_gather[dev])))
-            return rc;
-    } else if ((rc = ensure_smem_attr((const void*)gemm_bf16a_mxfp8_kernel<false>, P_SMEM_BYTES,
-                                      &g_smem_attr_bf16a[dev]))) {
-        return rc;
     }
     if (copy_b) {
         const cudaError_t ce = cudaMemcpy2DAsync(b_copy, (size_t)ldb * 2, B, (size_t)N * 2, (size_t)N * 2,
@@ -1760,6 +1860,18 @@ int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scale
             p.num_items = tiles + rem;
         }
     }
+    using TileLay = PLayout<P_TILE_STAGES, 0>;
+    using SkLay = PLayout<P_SK_STAGES, P_SK_SLOTS>;
+    const auto k_tiles = gemm_bf16a_mxfp8_kernel<false, P_TILE_STAGES, 0>;
+    const auto k_sk = gemm_bf16a_mxfp8_kernel<false, P_SK_STAGES, P_SK_SLOTS>;
+    const auto k_gather = gemm_bf16a_mxfp8_kernel<true, P_TILE_STAGES, 0>;
+    if (gather) {
+        if ((rc = ensure_smem_attr((const void*)k_gather, TileLay::SMEM_BYTES, &g_smem_attr_gather[dev]))) return rc;
+    } else if (p.sk_tiles > 0) {
+        if ((rc = ensure_smem_attr((const void*)k_sk, SkLay::SMEM_BYTES, &g_smem_attr_sk[dev]))) return rc;
+    } else if ((rc = ensure_smem_attr((const void*)k_tiles, TileLay::SMEM_BYTES, &g_smem_attr_bf16a[dev]))) {
+        return rc;
+    }
     cudaError_t e = launch_mxfp8_dequantize_bf16(A_data, A_scales, workspace, M, K, lda, stream, zero_words,
                                                  n_zero);
     if (e != cudaSuccess) {
@@ -1767,10 +1879,11 @@ int launch_gemm_mxfp8_bf16_prepass(const uint8_t* A_data, const uint8_t* A_scale
         return (int)e;
     }
     if (gather)
-        return launch_pair_kernel(gemm_bf16a_mxfp8_kernel<true>, P_SMEM_BYTES, P_THREADS, tmap_a16, tmap_b, p,
-                                  stream, true);
-    return launch_pair_kernel(gemm_bf16a_mxfp8_kernel<false>, P_SMEM_BYTES, P_THREADS, tmap_a16, tmap_b, p,
-                              stream, true, min_clusters);
+        return launch_pair_kernel(k_gather, TileLay::SMEM_BYTES, P_THREADS, tmap_a16, tmap_b, p, stream, true);
+    if (p.sk_tiles > 0)
+        return launch_pair_kernel(k_sk, SkLay::SMEM_BYTES, P_THREADS, tmap_a16, tmap_b, p, stream, true,
+                                  min_clusters);
+    return launch_pair_kernel(k_tiles, TileLay::SMEM_BYTES, P_THREADS, tmap_a16, tmap_b, p, stream, true);
 }
 
 int launch_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t epoch, cudaStream_t stream)

@@ -195,6 +195,22 @@ __device__ __forceinline__ void fence_proxy_async_smem()
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Order this thread's earlier generic-proxy accesses of global memory (an acquire of
+// data other SMs stored) before the async-proxy accesses it issues next (bulk copies).
+__device__ __forceinline__ void fence_proxy_async_global()
+{
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Bulk copy (no tensor map, no multicast) of `bytes` from global memory into this
+// CTA's shared memory, completing on an mbarrier of this CTA.  Both addresses
+// 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // tcgen05: tensor memory and the 5th-generation MMA
 // ---------------------------------------------------------------------------

@@ -26,7 +26,8 @@ def test_header_declares_the_reference_replacements():
     names = declared_symbols()
     for n in ("mpk_gemm_mxfp8_bf16", "mpk_mxfp8_quantize", "mpk_mxfp8_dequantize",
               "mpk_mxfp8_quantize_host", "mpk_mxfp8_dequantize_host", "mpk_status_string",
-              "mpk_last_error", "mpk_device_status"):
+              "mpk_last_error", "mpk_last_error_string", "mpk_device_status", "mpk_mxfp8_quantize_cols",
+              "mpk_mxfp8_quantize_bf16_cols", "mpk_set_gemm_schedule", "mpk_gemm_plan"):
         assert n in names, names
 
 
@@ -102,6 +103,11 @@ def test_argument_validation_without_a_device(mpk_lib):
     assert L.mpk_mxfp8_quantize(None, None, None, 4, -2, None) == MPK_ERR_INVALID_VALUE
     assert L.mpk_mxfp8_dequantize(None, None, None, 4, 0, None) == MPK_SUCCESS
     assert L.mpk_set_wait_timeout_ns(0) == MPK_ERR_INVALID_VALUE
+    assert L.mpk_mxfp8_quantize_cols(None, None, None, -1, 4, None) == MPK_ERR_INVALID_VALUE
+    assert L.mpk_mxfp8_quantize_cols(None, None, None, 0, 4, None) == MPK_SUCCESS
+    assert L.mpk_mxfp8_quantize_bf16_cols(None, None, None, 4, 4, None) == MPK_ERR_INVALID_VALUE
+    assert L.mpk_mxfp8_quantize_bf16_cols(3, 1 << 20, 1 << 20, 4, 4, None) == mpk_lib.MPK_ERR_MISALIGNED
+    assert L.mpk_last_error_string() == L.mpk_last_error() and b"aligned" in L.mpk_last_error_string()
     import torch
     if not torch.cuda.is_available():
         # well-formed arguments, but no sm_100 device: refused before any launch

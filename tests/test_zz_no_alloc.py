@@ -97,3 +97,23 @@ def test_oversize_is_rejected_before_any_launch(mpk_lib, cuda):
     torch.cuda.synchronize()
     assert bool((D == 0xEE).all()) and bool((Ds == 0xEE).all())
     assert mpk_lib.device_status() == 0
+
+
+def test_second_call_takes_no_device_memory(mpk_lib, cuda):
+    """After the first call on a device (which loads the library's device code that
+    holds the array), further calls leave the device's free memory unchanged."""
+    import torch
+
+    inp = O.make_gemm_inputs(512, 512, 512, seed=9)
+    D, S = _noalloc(mpk_lib, inp)  # first call: the array is reserved here at the latest
+    torch.cuda.synchronize()
+    A, As, B = to_dev(inp["A_data"]), to_dev(inp["A_scales"]), to_dev(inp["B_bf16"])
+    C, Cs = to_dev(inp["C_data"]), to_dev(inp["C_scales"])
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        mpk_lib.gemm_fp8_tensorcore_noalloc(A, As, B, C, Cs, D, S, 512, 512, 512)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
+    assert mpk_lib.device_status() == 0
