@@ -837,6 +837,11 @@ def run_codec_arm(args, world, rank, local, dist):
     qb_ms = timed(lambda: L.mpk_mxfp8_quantize_bf16(x16.data_ptr(), d.data_ptr(), s.data_ptr(), M, K, sptr))
     db_ms = timed(lambda: L.mpk_mxfp8_dequantize_bf16(d.data_ptr(), s.data_ptr(), x16.data_ptr(), M, K, sptr))
     bytes16 = M * K * 2 + M * K + M * K // 32
+    # Quantize with the blocks along the rows (32 rows per column): same traffic.
+    sc = torch.empty(((M + 31) // 32, K), dtype=torch.uint8, device="cuda")
+    qc_ms = timed(lambda: L.mpk_mxfp8_quantize_cols(x.data_ptr(), d.data_ptr(), sc.data_ptr(), M, K, sptr))
+    qcb_ms = timed(lambda: L.mpk_mxfp8_quantize_bf16_cols(x16.data_ptr(), d.data_ptr(), sc.data_ptr(), M, K, sptr))
+    del sc
     peaks, src = load_peaks()
     hbm = float(peaks["hbm_gbs"])
     qg, dg = bytes_one / q_ms / 1e6, bytes_one / dq_ms / 1e6
@@ -884,6 +889,11 @@ def run_codec_arm(args, world, rank, local, dist):
                             "dequantize_bf16_gbs": round(bytes16 / db_ms / 1e6, 1),
                             "dequantize_bf16_frac": round(bytes16 / db_ms / 1e6 / hbm, 4),
                             "bytes_per_launch": bytes16},
+        "row_blocks": {"what": "quantize with blocks of 32 rows per column (mpk_mxfp8_quantize_cols, _bf16_cols)",
+                       "quantize_cols_gbs": round(bytes_one / qc_ms / 1e6, 1),
+                       "quantize_cols_frac": round(bytes_one / qc_ms / 1e6 / hbm, 4),
+                       "quantize_bf16_cols_gbs": round(bytes16 / qcb_ms / 1e6, 1),
+                       "quantize_bf16_cols_frac": round(bytes16 / qcb_ms / 1e6 / hbm, 4)},
         "roofline": {"bound": "hbm", "achieved": round(qg, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(qg / hbm, 4), "traffic": load_traffic("mxfp8_quantize_flat_kernel", "codec"),
                      "peak_source": f"{src} hbm_gbs", "dequantize_gbs": round(dg, 1),

@@ -417,6 +417,60 @@ mxfp8_quantize_cols_kernel(const T* __restrict__ in, uint8_t* __restrict__ data,
     }
 }
 
+// BF16 source, 8 columns per thread: the 32 rows are held as packed BF16 (one
+// 16-byte load per row, 512 B per warp instruction) and widened where they are
+// used, so the registers hold the block twice as densely as FP32 would.
+__global__ void __launch_bounds__(kColsThreads)
+mxfp8_quantize_bf16_cols8_kernel(const uint16_t* __restrict__ in, uint8_t* __restrict__ data,
+                                 uint8_t* __restrict__ scales, int64_t M, int64_t K, int64_t ngroups,
+                                 int64_t nblocks)
+{
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; w < ngroups * nblocks; w += stride) {
+        const int64_t k0 = (w % ngroups) * 8;
+        const int64_t r0 = (w / ngroups) * 32;
+        const int rows = (int)min((int64_t)32, M - r0);
+        uint4 v[32];
+        const uint4* src = reinterpret_cast<const uint4*>(in + r0 * K + k0);
+        const int64_t step = K / 8;  // one row, in 16-byte units
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = i < rows ? __ldcs(src + i * step) : make_uint4(0u, 0u, 0u, 0u);
+        // Block amax on the packed BF16 bits: a magnitude's bits order like its value
+        // (non-negative floats), NaN magnitudes (above 0x7F80) are dropped as fmaxf
+        // drops them, and rows past M are zeros.
+        uint32_t amax2[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const uint32_t wd[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                const uint32_t m = wd[h] & 0x7FFF7FFFu;
+                amax2[h] = __vmaxu2(amax2[h], m & __vcmpleu2(m, 0x7F807F80u));
+            }
+        }
+        float inv[8];
+        uint32_t sc[2] = {0u, 0u};
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const float amax = __uint_as_float(c & 1 ? amax2[c >> 1] & 0xFFFF0000u : amax2[c >> 1] << 16);
+            sc[c >> 2] |= mx_block_scale(amax, inv[c]) << (8 * (c & 3));
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            if (i >= rows) break;
+            const uint32_t wd[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+            uint32_t q[4];
+#pragma unroll
+            for (int h = 0; h < 4; ++h)
+                q[h] = f32x2_to_e4m3x2(__uint_as_float(wd[h] << 16) * inv[2 * h],
+                                       __uint_as_float(wd[h] & 0xFFFF0000u) * inv[2 * h + 1]);
+            __stcs(reinterpret_cast<uint2*>(data + r0 * K + k0) + i * step,
+                   make_uint2(q[0] | (q[1] << 16), q[2] | (q[3] << 16)));
+        }
+        *reinterpret_cast<uint2*>(scales + (r0 / 32) * K + k0) = make_uint2(sc[0], sc[1]);
+    }
+}
+
 // ------------------------------- launchers ---------------------------------
 
 static int codec_grid(int64_t work_items)
@@ -495,7 +549,19 @@ cudaError_t launch_mxfp8_quantize_cols(const float* in, uint8_t* data, uint8_t* 
 cudaError_t launch_mxfp8_quantize_bf16_cols(const void* in, uint8_t* data, uint8_t* scales, int64_t M,
                                             int64_t K, cudaStream_t stream)
 {
-    return launch_quantize_cols<uint16_t>(static_cast<const uint16_t*>(in), data, scales, M, K, stream);
+    const uint16_t* x = static_cast<const uint16_t*>(in);
+    if (M == 0 || K == 0) return cudaSuccess;
+    if (K % 8 == 0 && aligned16(in) && (reinterpret_cast<uintptr_t>(data) & 7u) == 0 &&
+        (reinterpret_cast<uintptr_t>(scales) & 7u) == 0) {
+        const int64_t nblocks = (M + 31) / 32, ngroups = K / 8;
+        int64_t blocks = (ngroups * nblocks + kColsThreads - 1) / kColsThreads;
+        const int64_t cap = (int64_t)device_sm_count() * 32;
+        if (blocks > cap) blocks = cap;
+        mxfp8_quantize_bf16_cols8_kernel<<<(int)blocks, kColsThreads, 0, stream>>>(x, data, scales, M, K, ngroups,
+                                                                                  nblocks);
+        return cudaGetLastError();
+    }
+    return launch_quantize_cols<uint16_t>(x, data, scales, M, K, stream);
 }
 
 cudaError_t launch_mxfp8_dequantize(const uint8_t* data, const uint8_t* scales, float* out,

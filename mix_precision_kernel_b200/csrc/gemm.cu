@@ -1691,14 +1691,15 @@ SkPlan gemm_sk_plan(int M, int N, int K)
     // Auto: the tiles of the last, partial wave are spread over the clusters when
     // that gives each cluster at least kSkMinIters K-steps and more clusters than
     // whole tiles would keep busy, and when the partial wave is a large part of the
-    // run: one to three full waves before it, and it at most 85 % full.  The owners'
-    // merge of the partials (L2-latency bound, overlapped with the next whole tiles)
-    // costs more than it saves with no full wave to overlap it, and with many waves
-    // or a nearly full last wave the gain is within that cost (measured on B200:
-    // +6 to +19 % at 1.5-3.5 waves, -4 to -19 % outside that band).
+    // run: one to three full waves, at least 128 K-steps of whole tiles per cluster
+    // after the spread ones, and a last wave at most 85 % full.  The contributors'
+    // stores and the owners' merge of the partials share each SM's L2 port with the
+    // whole tiles' loads; with fewer whole K-steps to hide behind, with many waves or
+    // with a nearly full last wave they cost about what they save (measured on B200:
+    // +4 to +20 % inside these bounds, -4 to -19 % outside them).
     const int64_t rem = tiles % clusters;
     const int64_t waves = tiles / clusters;
-    if (rem == 0 || waves < 1 || waves > 3 || rem * 100 > clusters * 85) return plan;
+    if (rem == 0 || waves < 1 || waves > 3 || waves * kb < 128 || rem * 100 > clusters * 85) return plan;
     const int64_t csk = std::min(clusters, rem * kb / kSkMinIters);
     if (csk <= rem) return plan;
     plan.tiles = (int)rem;

@@ -98,14 +98,15 @@ def test_library_plan_walks_cleanly(mpk_lib, M, N, K):
 
 
 def test_plan_of_the_scaling_shapes(mpk_lib):
-    """On 74 SM pairs: the dense projection on 8 GPUs (512 rows each) has 96 tiles,
-    1 full wave + 22; those 22 tiles' 1408 K-steps go to all 74 pairs; on 4 GPUs
-    (1024 rows) 2 waves + 44.  The wide shape on 8 GPUs (3584 columns each): 1 wave
-    + 38.  Products with no full wave, more than three, a last wave over 85 % full,
-    whole waves only, or a spread that would leave under 8 K-steps per pair keep
-    whole tiles."""
-    assert mpk_lib.gemm_plan(512, 12288, 4096) == (96, 22, 74)
+    """On 74 SM pairs: the dense projection on 4 GPUs (1024 rows each) has 192
+    tiles, 2 full waves + 44; those 44 tiles' 2816 K-steps go to all 74 pairs.  The
+    wide shape on 8 GPUs (3584 columns each): 1 wave of 128 K-steps + 38.  Products
+    with no full wave, more than three, fewer than 128 whole K-steps per pair (the
+    dense projection on 8 GPUs: 1 wave of 64), a last wave over 85 % full, whole
+    waves only, or a spread that would leave under 8 K-steps per pair keep whole
+    tiles."""
     assert mpk_lib.gemm_plan(1024, 12288, 4096) == (192, 44, 74)
+    assert mpk_lib.gemm_plan(512, 12288, 4096) == (96, 0, 0)
     assert mpk_lib.gemm_plan(2048, 3584, 8192) == (112, 38, 74)
     assert mpk_lib.gemm_plan(128, 4096, 4096) == (16, 0, 0)       # no full wave
     assert mpk_lib.gemm_plan(4096, 12288, 4096) == (768, 0, 0)    # ten waves
@@ -114,7 +115,7 @@ def test_plan_of_the_scaling_shapes(mpk_lib):
     assert mpk_lib.gemm_plan(256, 256 * 74, 4096) == (74, 0, 0)   # one full wave
     prev = mpk_lib.set_gemm_schedule(mpk_lib.SCHEDULE_TILES)
     try:
-        assert mpk_lib.gemm_plan(512, 12288, 4096) == (96, 0, 0)
+        assert mpk_lib.gemm_plan(1024, 12288, 4096) == (192, 0, 0)
         mpk_lib.set_gemm_schedule(mpk_lib.SCHEDULE_STREAM_K)
         assert mpk_lib.gemm_plan(512, 512, 512) == (4, 4, 32)
     finally:
@@ -123,7 +124,7 @@ def test_plan_of_the_scaling_shapes(mpk_lib):
 
 
 def test_workspace_size_includes_the_partials(mpk_lib):
-    M, N, K = 512, 12288, 4096
+    M, N, K = 1024, 12288, 4096
     base = M * K * 2
     size = mpk_lib.gemm_workspace_size(M, N, K)
     assert size >= base + 74 * 2 * 128 * 256 * 4

@@ -50,12 +50,12 @@ def _against_tiles(mpk, inp, label, with_c=True, rows=None):
     assert mpk.device_status() == 0
 
 
-@pytest.mark.parametrize("M,N,K", [(1024, 5632, 640), (1024, 12288, 1024), (512, 12288, 4096),
-                                   (1024, 12288, 4096), (2048, 3584, 8192)])
+@pytest.mark.parametrize("M,N,K", [(1024, 10240, 4096), (768, 7680, 8192), (1024, 12288, 4096),
+                                   (2048, 3584, 8192), (2048, 7168, 8192)])
 def test_default_schedule_split_wave(mpk_lib, cuda, M, N, K):
     """Shapes whose default plan spreads the last wave's tiles over the SM pairs,
-    among them the per-GPU slabs of the dense projection on 8 and 4 GPUs and of the
-    wide shape on 8 GPUs."""
+    among them the per-GPU slabs of the dense projection on 4 GPUs and of the wide
+    shape on 8 and 4 GPUs."""
     tiles, sk_tiles, pairs = mpk_lib.gemm_plan(M, N, K)
     assert sk_tiles > 0 and pairs > sk_tiles, (tiles, sk_tiles, pairs)
     inp = O.make_gemm_inputs(M, N, K, seed=M + N + K)
