@@ -13,7 +13,7 @@
 //                            arrive by TMA.  Optionally forwards D tiles to other
 //                            GPUs (the fused all-gather).
 //   gemm_mxfp8_bf16_kernel   (the allocation-free variant) A arrives as E4M3 codes
-//                            and transform warps convert it to BF16 in shared memory.
+//                            and transform warps convert it to BF16 in tensor memory.
 //
 // Work decomposition.  Clusters of two CTAs on neighbouring SMs own 256 x 256
 // output tiles (persistent, work items strided by the number of clusters, in the
@@ -21,22 +21,26 @@
 // items, item_coords).  CTA rank r of the pair owns output rows [m0 + 128 r, +128)
 // and loads only its half of the tile's B columns, [n0 + 128 r, +128): the pair MMA
 // (tcgen05.mma.cta_group::2, M=256 N=256 K=16, issued by rank 0) reads A rows from
-// each CTA's own shared memory and B columns from both, and writes each CTA's
-// 128 x 256 FP32 accumulator into that CTA's tensor memory.  Versus one CTA per
-// 128 x 256 tile this halves the B bytes each SM pulls from L2 per MMA.
+// each CTA (its shared memory, or in the on-chip variant its tensor memory) and B
+// columns from both CTAs' shared memory, and writes each CTA's 128 x 256 FP32
+// accumulator into that CTA's tensor memory.  Versus one CTA per 128 x 256 tile
+// this halves the B bytes each SM pulls from L2 per MMA.
 //
-// On-chip variant, per CTA and per K-step of 64 (STAGES-deep ring):
-//   A codes  u8   128 x 64   8 KiB  TMA (64-byte swizzle), completes on this CTA's full_a8
-//   A bf16        128 x 64  16 KiB  written by the transform warps, K-major, 128-byte
-//                                   swizzle (the UMMA canonical layout)
-//   B bf16         64 x 128 16 KiB  TMA, two 64x64 boxes, 128-byte swizzle, MN-major;
-//                                   completes on rank 0's full_b (.cta_group::2)
+// On-chip variant, per CTA and per K-step of 64:
+//   A codes  u8   128 x 64   8 KiB  TMA (64-byte swizzle) into a ring of A8_STAGES,
+//                                   completes on this CTA's a8_full
+//   B bf16         64 x 128 16 KiB  TMA, two 64x64 boxes, 128-byte swizzle, MN-major,
+//                                   into a ring of STAGES (.cta_group::2: completes on
+//                                   rank 0's full)
+//   A bf16        128 x 64  32 TMEM columns (lane = row, two BF16 per column), written
+//                                   by the transform warps with tcgen05.st into the
+//                                   stage of the same ring; arrives on rank 0's full
 // Warp roles of the on-chip variant (per CTA):
-//   warp 0   TMA producer (one lane)
+//   warp 0   B producer (one lane); warp 2 A-code producer (one lane)
 //   warp 1   TMEM owner (cta_group::2 allocation); on rank 0 also the MMA issuer
-//   warps 2+ transform: E4M3 code x 2^(scale-127) -> BF16 in shared memory (exact for
-//            scale bytes 3..246), then fence.proxy.async and an arrive on rank 0's
-//            full_a16 barrier
+//   warps 4-11 transform, two groups of 4 alternating K-steps: E4M3 code x
+//            2^(scale-127) -> BF16 (exact for scale bytes 3..246), tcgen05.st, then
+//            an arrive on rank 0's full
 //   last 4   epilogue: tcgen05.ld of this CTA's accumulator rows, + dequantized C,
 //            per-32-column amax, E8M0 scale, RNE E4M3, 16-byte stores
 // (The BF16-A kernel's ring and roles are described at its definition.)
@@ -72,9 +76,11 @@ constexpr int BN = 256;        // output columns per tile (each CTA loads BN/2 o
 constexpr int BN_HALF = BN / 2;
 constexpr int BK = 64;
 #ifndef MPK_STAGES
-#define MPK_STAGES 5
+#define MPK_STAGES 8
 #endif
-constexpr int STAGES = MPK_STAGES;      // ring of B halves + BF16 A tiles (consumed by the MMA)
+// On-chip variant: ring of K-steps consumed by the MMA (a B half in shared memory and
+// the converted BF16 A tile in tensor memory per stage).
+constexpr int STAGES = MPK_STAGES;
 #ifndef MPK_A8_STAGES
 #define MPK_A8_STAGES 8
 #endif
@@ -107,7 +113,7 @@ constexpr int kThreads = 32 * (kFirstEpilogueWarp + kEpilogueWarps);
 // (checked below), and the launcher verifies the compiled register count before
 // it launches, so setmaxnreg.inc can always be satisfied.
 constexpr int kLaunchRegs = (65536 / kThreads) / 8 * 8 > 255 ? 248 : (65536 / kThreads) / 8 * 8;
-constexpr int kCtrlRegs = 40;
+constexpr int kCtrlRegs = 48;
 constexpr int kXformRegs = kTransformGroups == 4 ? 72 : kLaunchRegs;
 constexpr int kEpiRegs = (kThreads * kLaunchRegs - 128 * kCtrlRegs - 32 * kTransformWarps * kXformRegs) /
                          128 / 8 * 8 > 248 ? 248
@@ -123,15 +129,23 @@ constexpr int A8_BYTES = BM * BK;               // 8192
 constexpr int A16_BYTES = BM * BK * 2;          // 16384
 constexpr int B_BOX_BYTES = 64 * BK * 2;        // one 64(N) x 64(K) box: 8192
 constexpr int B_BYTES = BK * BN_HALF * 2;       // 16384 per CTA
-constexpr uint32_t kTmemCols = 2 * BN;          // two FP32 accumulators of BN columns
+constexpr uint32_t kTmemCols = 2 * BN;          // all 512 columns of tensor memory
+
+// On-chip variant's tensor memory (per CTA, 128 lanes = the CTA's 128 tile rows):
+// one FP32 accumulator of BN columns, then the BF16 A ring: one stage per K-step,
+// 32 columns (64 BF16 of a row, two per 32-bit column).  Pair MMAs of N = 128 (two
+// per K slice into two half accumulators) run at about two thirds of the rate of
+// N = 256 on B200, so the tile keeps one N = 256 accumulator and the epilogue's
+// drain is not overlapped with the next tile's MMAs.
+constexpr uint32_t kTmemACol = BN;
+constexpr uint32_t kTmemAStageCols = BK / 2;
+static_assert(kTmemACol + STAGES * kTmemAStageCols <= kTmemCols, "tensor memory holds 512 columns");
 
 constexpr int OFF_B = 0;
-constexpr int OFF_A16 = OFF_B + STAGES * B_BYTES;
-constexpr int OFF_A8 = OFF_A16 + STAGES * A16_BYTES;
+constexpr int OFF_A8 = OFF_B + STAGES * B_BYTES;
 constexpr int OFF_BAR = OFF_A8 + A8_STAGES * A8_BYTES;
-// barriers: a8_full[S8], a8_empty[S8], full_b[S], full_a16[S], empty[S], tfull[2],
-// tempty[2], drain
-constexpr int kNumBars = 2 * A8_STAGES + 3 * STAGES + 5;
+// barriers: a8_full[S8], a8_empty[S8], full[S], empty[S], tfull, tempty, drain
+constexpr int kNumBars = 2 * A8_STAGES + 2 * STAGES + 3;
 constexpr int OFF_MISC = OFF_BAR + kNumBars * 8;
 constexpr int SMEM_USED = OFF_MISC + 16;
 constexpr int SMEM_BYTES = SMEM_USED + 1024;  // slack for 1024-byte alignment
@@ -468,97 +482,73 @@ __device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b)
     return d;
 }
 
-// 16 E4M3 codes sharing one E8M0 scale byte s -> 16 BF16 (two 16-byte chunks).
-//
-// Fast path (scale bytes 3..134, no NaN code): each code's sign and 7 magnitude
-// bits are moved into a BF16 bit pattern equal to code x 2^-120 (the E4M3
-// exponent bits land in the low BF16 exponent bits; E4M3 subnormals become BF16
-// subnormals), then one BF16 multiply by 2^(s-7) -- a power of two, so exact --
-// gives code x 2^(s-127).  Integer ops and mul.rn.bf16x2 only.
-// Slow path (any scale, NaN codes): E4M3 -> f16 -> f32 with hardware conversions,
-// multiply by the FP32 scale (0 -> 0.0, 255 -> inf as in the reference), round to
-// BF16.  Both paths are exact wherever the product is representable in BF16
-// (scale bytes 3..246).
-// One row of one K-step: 64 E4M3 codes (four 16-code chunks) with the
-// E8M0 scale bytes s0 (codes 0..31) and s1 (codes 32..63) -> 64 BF16 written as
-// eight 16-byte chunks into the 128B-swizzled row at `row` (chunk c lands at
-// ((c ^ xr) << 4)).  Chunks at K offset >= kvalid are written as zeros.
+// One row of one K-step of the on-chip variant: 64 E4M3 codes with the E8M0 scale
+// bytes s0 (codes 0..31) and s1 (codes 32..63) -> 64 BF16, packed two per 32-bit
+// word in K order (word j = codes 2j, 2j+1, the lower one in the low half), which is
+// the row's layout in a tensor-memory A operand (lane = row, 32-bit column j).
 //
 // Exact general path: E4M3 -> f16 -> f32 with hardware conversions, multiply by
 // the FP32 scale (byte 0 -> 0.0 and 255 -> inf, as in the reference), round to
-// BF16.  Used for scale bytes outside 3..134, NaN codes and the K tail; kept out of
-// line so the hot loop stays small.
-__device__ __noinline__ void transform_row_exact(const uint8_t* a8row, uint32_t a8xr, uint32_t s0,
-                                                 uint32_t s1, uint8_t* row, uint32_t xr, int kvalid)
+// BF16; codes at K offset >= kvalid become zeros.  Used for scale bytes outside
+// 3..134, NaN codes and the K tail; kept out of line so the hot loop stays small.
+__device__ __noinline__ void convert_row_exact(const uint8_t* a8row, uint32_t a8xr, uint32_t s0, uint32_t s1,
+                                               int kvalid, uint32_t* out)
 {
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
-        uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-        if (16 * c < kvalid) {
-            // The codes are re-read from the A-code tile (64-byte swizzled row).
-            const uint4 qc = *reinterpret_cast<const uint4*>(a8row + ((((uint32_t)c) ^ a8xr) << 4));
-            const uint32_t in[4] = {qc.x, qc.y, qc.z, qc.w};
-            const float scale = e8m0_to_f32(c < 2 ? s0 : s1);
+        // Chunk c (codes 16c .. 16c+15), re-read from the 64-byte swizzled code row.
+        const uint4 qc = *reinterpret_cast<const uint4*>(a8row + ((((uint32_t)c) ^ a8xr) << 4));
+        const uint32_t in[4] = {qc.x, qc.y, qc.z, qc.w};
+        const float scale = e8m0_to_f32(c < 2 ? s0 : s1);
 #pragma unroll
-            for (int w = 0; w < 4; ++w) {
+        for (int w = 0; w < 4; ++w) {
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const float2 f = e4m3x2_to_f32x2(in[w] >> (16 * h));
-                    uint32_t packed;
-                    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed) : "f"(f.y * scale), "f"(f.x * scale));
-                    out[2 * w + h] = packed;
-                }
+            for (int h = 0; h < 2; ++h) {
+                const int k = 16 * c + 4 * w + 2 * h;  // K offset of the pair's first code
+                const float2 f = e4m3x2_to_f32x2(in[w] >> (16 * h));
+                const float lo = k < kvalid ? f.x * scale : 0.0f;
+                const float hi = k + 1 < kvalid ? f.y * scale : 0.0f;
+                uint32_t packed;
+                asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed) : "f"(hi), "f"(lo));
+                out[8 * c + 2 * w + h] = packed;
             }
         }
-        *reinterpret_cast<uint4*>(row + ((((uint32_t)(2 * c)) ^ xr) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
-        *reinterpret_cast<uint4*>(row + ((((uint32_t)(2 * c + 1)) ^ xr) << 4)) = make_uint4(out[4], out[5], out[6], out[7]);
     }
 }
 
-// Fast path for one row of one K-step (same contract as transform_row_exact, with
-// the four code chunks already loaded into q[0..3]),
-// valid when both scale bytes are in 3..134, no code is NaN (0x7F/0xFF) and all 64
-// codes are inside K.  Each code's sign and 7 magnitude bits are moved into a BF16
-// bit pattern equal to code x 2^-120 (the E4M3 exponent bits land in the low BF16
-// exponent bits; E4M3 subnormals become BF16 subnormals); one BF16 multiply by
-// 2^(s-7) -- a power of two, so exact -- gives code x 2^(s-127).  Integer ops and
-// mul.rn.bf16x2 only, straight-line over the four chunks.  Returns false (writing
-// nothing) when the preconditions do not hold.
-__device__ __forceinline__ bool transform_row_fast(const uint4* q, uint32_t s0, uint32_t s1, uint8_t* row,
-                                                   uint32_t xr, int kvalid)
+// Fast path for one row of one K-step (same contract as convert_row_exact), valid
+// when both scale bytes are in 3..134, no code is NaN (0x7F/0xFF) and all 64 codes
+// are inside K: fast_row_ok checks this on the four 16-code chunks q[0..3], and
+// convert_half_fast converts 32 codes (two chunks, one scale byte s) to 16 words.
+// Each code's sign and 7 magnitude bits are moved into a BF16 bit pattern equal to
+// code x 2^-120 (the E4M3 exponent bits land in the low BF16 exponent bits; E4M3
+// subnormals become BF16 subnormals); one BF16 multiply by 2^(s-7) -- a power of
+// two, so exact -- gives code x 2^(s-127).  Integer ops and mul.rn.bf16x2 only.
+__device__ __forceinline__ bool fast_row_ok(const uint4 (&q)[4], uint32_t s0, uint32_t s1, int kvalid)
 {
-    uint32_t wm[16], nan_probe = 0u;
+    uint32_t nan_probe = 0u;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
         const uint32_t in[4] = {q[c].x, q[c].y, q[c].z, q[c].w};
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            wm[4 * c + w] = in[w] & 0x7F7F7F7Fu;
-            nan_probe |= wm[4 * c + w] + 0x01010101u;  // a byte 0x7F becomes 0x80
-        }
+        for (int w = 0; w < 4; ++w) nan_probe |= (in[w] & 0x7F7F7F7Fu) + 0x01010101u;  // 0x7F -> 0x80
     }
-    if ((s0 - 3u) > 131u || (s1 - 3u) > 131u || (nan_probe & 0x80808080u) != 0u || kvalid < 64)
-        return false;
-    uint32_t f0 = (s0 + 120u) << 7, f1 = (s1 + 120u) << 7;  // BF16 2^(s-7)
-    f0 |= f0 << 16;
-    f1 |= f1 << 16;
+    return (s0 - 3u) <= 131u && (s1 - 3u) <= 131u && (nan_probe & 0x80808080u) == 0u && kvalid >= 64;
+}
+
+__device__ __forceinline__ void convert_half_fast(uint4 qa, uint4 qb, uint32_t s, uint32_t (&out)[16])
+{
+    uint32_t f = (s + 120u) << 7;  // BF16 2^(s-7)
+    f |= f << 16;
+    const uint32_t in[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        const uint32_t in[4] = {q[c].x, q[c].y, q[c].z, q[c].w};
-        const uint32_t f = c < 2 ? f0 : f1;
-        uint32_t out[8];
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            const uint32_t ws = in[w] & 0x80808080u;
-            const uint32_t m01 = prmt(wm[4 * c + w], 0u, 0x4140u), s01 = prmt(ws, 0u, 0x1404u);
-            const uint32_t m23 = prmt(wm[4 * c + w], 0u, 0x4342u), s23 = prmt(ws, 0u, 0x3424u);
-            out[2 * w] = mul_bf16x2(m01 * 16u + s01, f);
-            out[2 * w + 1] = mul_bf16x2(m23 * 16u + s23, f);
-        }
-        *reinterpret_cast<uint4*>(row + ((((uint32_t)(2 * c)) ^ xr) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
-        *reinterpret_cast<uint4*>(row + ((((uint32_t)(2 * c + 1)) ^ xr) << 4)) = make_uint4(out[4], out[5], out[6], out[7]);
+    for (int w = 0; w < 8; ++w) {
+        const uint32_t wm = in[w] & 0x7F7F7F7Fu, ws = in[w] & 0x80808080u;
+        const uint32_t m01 = prmt(wm, 0u, 0x4140u), s01 = prmt(ws, 0u, 0x1404u);
+        const uint32_t m23 = prmt(wm, 0u, 0x4342u), s23 = prmt(ws, 0u, 0x3424u);
+        out[2 * w] = mul_bf16x2(m01 * 16u + s01, f);
+        out[2 * w + 1] = mul_bf16x2(m23 * 16u + s23, f);
     }
-    return true;
 }
 
 // Epilogue math for one MX block of 32 accumulator values of one row.
@@ -619,6 +609,23 @@ __device__ __noinline__ bool epilogue_ragged_chunk(const Params& p, uint32_t tad
         p.D_scales[soff] = (uint8_t)sd;
     }
     return true;
+}
+
+// Adds one full 32-column chunk of C (32 E4M3 codes in c0, c1 and their scale
+// byte) to the accumulator values v.
+__device__ __forceinline__ void add_c_chunk(float (&v)[32], uint4 c0, uint4 c1, uint32_t cscale)
+{
+    const float sc = e8m0_to_f32(cscale);
+    const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        const float2 lo = e4m3x2_to_f32x2(cw[w]);
+        const float2 hi = e4m3x2_to_f32x2(cw[w] >> 16);
+        v[4 * w + 0] += lo.x * sc;
+        v[4 * w + 1] += lo.y * sc;
+        v[4 * w + 2] += hi.x * sc;
+        v[4 * w + 3] += hi.y * sc;
+    }
 }
 
 // One full 32-column D chunk (two 16-byte stores) and its scale byte, into this
@@ -799,20 +806,7 @@ __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base
                             break;
                         }
                     }
-                    if (has_c) {
-                        const float sc = e8m0_to_f32(cs[ci]);
-                        const uint32_t cw[8] = {cq[ci][0].x, cq[ci][0].y, cq[ci][0].z, cq[ci][0].w,
-                                                cq[ci][1].x, cq[ci][1].y, cq[ci][1].z, cq[ci][1].w};
-#pragma unroll
-                        for (int w = 0; w < 8; ++w) {
-                            const float2 lo = e4m3x2_to_f32x2(cw[w]);
-                            const float2 hi = e4m3x2_to_f32x2(cw[w] >> 16);
-                            v[4 * w + 0] += lo.x * sc;
-                            v[4 * w + 1] += lo.y * sc;
-                            v[4 * w + 2] += hi.x * sc;
-                            v[4 * w + 3] += hi.y * sc;
-                        }
-                    }
+                    if (has_c) add_c_chunk(v, cq[ci][0], cq[ci][1], cs[ci]);
                     uint4 d0, d1;
                     const uint32_t sd = quantize_block32(v, d0, d1);
                     if (row_ok) store_d_chunk<kGather>(p, grow, col0, d0, d1, sd);
@@ -855,6 +849,81 @@ __device__ __forceinline__ void run_epilogue(const Params& p, uint32_t tmem_base
     }
 }
 
+// Epilogue of the on-chip variant (4 warps, one thread per accumulator row): for
+// every tile of this cluster, wait for the accumulator, add the dequantized C,
+// quantize D to MXFP8 along N, store it, and release the accumulator on rank 0's
+// tempty barrier.
+__device__ __forceinline__ void run_epilogue_onchip(const Params& p, uint32_t tmem_base, uint32_t tfull,
+                                                    uint32_t tempty_rank0, int cluster, int nclusters,
+                                                    uint32_t rank, int warp, int lane, volatile int* abort_flag)
+{
+    const int quad = warp & 3;       // TMEM lanes this warp may access
+    const int r = quad * 32 + lane;  // accumulator row within this CTA's tile
+    const bool has_c = p.C_data != nullptr;
+    const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+    int it = 0;
+    for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
+        int m0, n0;
+        tile_coords(p, tile, m0, n0);
+        const int64_t grow = (int64_t)m0 + BM * (int)rank + r;
+        const bool row_ok = grow < p.M;
+        const int nchunks = min(BN / 32, (p.N - n0 + 31) / 32);
+        // This row's C codes and scales for the whole tile, loaded before the
+        // accumulator is ready so that the loads overlap the mainloop.
+        uint4 cq[BN / 32][2];
+        uint32_t cs[BN / 32];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+            cq[c][0] = cq[c][1] = make_uint4(0u, 0u, 0u, 0u);
+            cs[c] = 0u;
+            const int col0 = n0 + 32 * c;
+            if (has_c && row_ok && c < nchunks) {
+                cs[c] = __ldg(p.C_scales + grow * p.nblkN + col0 / 32);
+                if (p.vec_cd && col0 + 32 <= p.N) {
+                    const uint4* src = reinterpret_cast<const uint4*>(p.C_data + grow * p.N + col0);
+                    cq[c][0] = __ldg(src);
+                    cq[c][1] = __ldg(src + 1);
+                }
+            }
+        }
+        if (!mbar_wait(tfull, (uint32_t)it & 1u, abort_flag, p.status, kSiteTmemFull, p.timeout_ns)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+            if (c >= nchunks) break;  // warp-uniform: tcgen05.ld is warp-collective
+            const int col0 = n0 + 32 * c;
+            const int valid = min(32, p.N - col0);
+            const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(32 * c);
+            if (valid == 32 && p.vec_cd) {
+                uint32_t raw[32];
+                tmem_ld_32x32b_x32(taddr, raw);
+                tmem_ld_wait();
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]);
+                if (has_c) add_c_chunk(v, cq[c][0], cq[c][1], cs[c]);
+                uint4 d0, d1;
+                const uint32_t sd = quantize_block32(v, d0, d1);
+                if (row_ok) store_d_chunk<false>(p, grow, col0, d0, d1, sd);
+            } else {
+                // No partials to merge here: the chunk cannot give up.
+                epilogue_ragged_chunk<false>(p, taddr, cs[c], has_c, row_ok, grow, col0, valid, nullptr, 0, c, r,
+                                             abort_flag);
+            }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(tempty_rank0);
+    }
+}
+
+// On-chip variant.  Per CTA and K-step: the TMA producer brings this CTA's 128 x 64
+// A codes (64-byte swizzle) and its half of the tile's B columns (two 64-column
+// boxes, tile columns 128 rank .. +127);
+// a transform group converts the codes to BF16 and stores them into the A stage in
+// tensor memory (tcgen05.st, lane = row); rank 0 issues the pair MMAs
+// (tcgen05.mma.cta_group::2, A from tensor memory, B from shared memory, M = 256,
+// N = 256) into the accumulator.
 __global__ void __maxnreg__(kLaunchRegs)
 gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                        const __grid_constant__ CUtensorMap tmap_b, const Params p)
@@ -867,13 +936,16 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
     const uint32_t bar0 = sbase + OFF_BAR;
     auto a8_full = [&](int j) { return bar0 + 8u * j; };
     auto a8_empty = [&](int j) { return bar0 + 8u * (A8_STAGES + j); };
+    // Stage s of the MMA ring completes on rank 0's full(s) when both CTAs' B boxes
+    // have landed (TMA transaction bytes) and both CTAs' transform groups have stored
+    // the converted A; one MMA commit to empty(s) in both CTAs frees the B slot and
+    // the A stage together.
     const uint32_t barS = bar0 + 8u * (2 * A8_STAGES);
-    auto full_b = [&](int s) { return barS + 8u * s; };
-    auto full_a16 = [&](int s) { return barS + 8u * (STAGES + s); };
-    auto empty = [&](int s) { return barS + 8u * (2 * STAGES + s); };
-    auto tfull = [&](int a) { return barS + 8u * (3 * STAGES + a); };
-    auto tempty = [&](int a) { return barS + 8u * (3 * STAGES + 2 + a); };
-    const uint32_t drain = barS + 8u * (3 * STAGES + 4);
+    auto full = [&](int s) { return barS + 8u * s; };
+    auto empty = [&](int s) { return barS + 8u * (STAGES + s); };
+    const uint32_t tfull = barS + 8u * (2 * STAGES);
+    const uint32_t tempty = tfull + 8u;
+    const uint32_t drain = tfull + 16u;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
     // Stays 0: the abort flag of the teardown waits, which must not be cut short.
@@ -892,14 +964,12 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
             mbar_init(a8_empty(j), 4);  // the 4 warps of the transform group that read it
         }
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(full_b(s), 1);
-            mbar_init(full_a16(s), 2 * 4);  // one transform group per stage, both CTAs
+            // rank 0's B producer (expect_tx) + one transform group per stage, both CTAs
+            mbar_init(full(s), 1 + 2 * 4);
             mbar_init(empty(s), 1);
         }
-        for (int a = 0; a < 2; ++a) {
-            mbar_init(tfull(a), 1);
-            mbar_init(tempty(a), 2 * kEpilogueWarps);
-        }
+        mbar_init(tfull, 1);
+        mbar_init(tempty, 2 * kEpilogueWarps);
         mbar_init(drain, 1);
         *abort_flag = 0;
         *never_abort = 0;
@@ -928,19 +998,18 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
             for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
                 int m0, n0;
                 tile_coords(p, tile, m0, n0);
-                const int col0 = n0 + BN_HALF * (int)rank;
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, p.status, kSiteEmpty, p.timeout_ns)) {
                         ok = false;
                         break;
                     }
-                    // B halves of both CTAs complete on rank 0's full_b.
-                    if (rank == 0) mbar_arrive_expect_tx(full_b(s), 2 * B_BYTES);
-                    const uint32_t fb = mapa_shared(full_b(s), 0);
+                    // B boxes of both CTAs complete on rank 0's full.
+                    if (rank == 0) mbar_arrive_expect_tx(full(s), 2 * B_BYTES);
+                    const uint32_t fb = mapa_shared(full(s), 0);
 #pragma unroll
                     for (int j = 0; j < BN_HALF / 64; ++j)
                         tma_load_2d_pair(sbase + OFF_B + s * B_BYTES + j * B_BOX_BYTES, &tmap_b, fb,
-                                         col0 + 64 * j, kb * BK);
+                                         n0 + BN_HALF * (int)rank + 64 * j, kb * BK);
                     ++issued;
                     if (++s == STAGES) { s = 0; ph ^= 1u; }
                 }
@@ -953,7 +1022,7 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 uint32_t pp = ph;
                 for (int i = 0; i < outstanding; ++i) {
                     if (--ss < 0) { ss = STAGES - 1; pp ^= 1u; }
-                    if (rank == 0) mbar_wait(full_b(ss), pp, never_abort, nullptr, 0, kDrainTimeoutNs);
+                    if (rank == 0) mbar_wait(full(ss), pp, never_abort, nullptr, 0, kDrainTimeoutNs);
                 }
             }
         }
@@ -999,39 +1068,34 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
             int it = 0;
             bool ok = true;
             for (int tile = cluster; ok && tile < num_tiles; tile += nclusters, ++it) {
-                const int acc = it & 1;
-                const uint32_t acc_ph = (uint32_t)(it >> 1) & 1u;
-                if (!mbar_wait(tempty(acc), acc_ph ^ 1u, abort_flag, p.status, kSiteTmemEmpty,
+                if (!mbar_wait(tempty, ((uint32_t)it & 1u) ^ 1u, abort_flag, p.status, kSiteTmemEmpty,
                                p.timeout_ns)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
-                    if (!mbar_wait(full_b(s), ph, abort_flag, p.status, kSiteFullB, p.timeout_ns) ||
-                        !mbar_wait(full_a16(s), ph, abort_flag, p.status, kSiteFullA16, p.timeout_ns)) {
+                    if (!mbar_wait(full(s), ph, abort_flag, p.status, kSiteFullB, p.timeout_ns)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = sbase + OFF_A16 + s * A16_BYTES;
+                    const uint32_t a_tmem = tmem_base + kTmemACol + (uint32_t)s * kTmemAStageCols;
                     const uint32_t b_addr = sbase + OFF_B + s * B_BYTES;
 #pragma unroll
                     for (int k = 0; k < BK / UMMA_K; ++k) {
-                        // A: K-major, 128-byte rows, 8-row groups 1024 B apart; a K step of
-                        // 16 elements is 32 bytes inside the swizzle atom.
-                        const uint64_t adesc = umma_smem_desc_sw128(a_addr + k * UMMA_K * 2, 16, 1024);
                         // B: MN-major, 64-column chunks 8 KiB apart (LBO), 8-row K groups
-                        // 1024 B apart (SBO); a K step of 16 rows is 2 KiB.
+                        // 1024 B apart (SBO); a K step of 16 rows is 2 KiB.  A: a K step of
+                        // 16 BF16 is 8 tensor-memory columns.
                         const uint64_t bdesc = umma_smem_desc_sw128(b_addr + k * UMMA_K * 128, B_BOX_BYTES, 1024);
-                        umma_bf16_pair(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0 ? 1u : 0u);
+                        umma_bf16_pair_tmem_a(tmem_base, a_tmem + (uint32_t)(k * UMMA_K / 2), bdesc, kIdesc,
+                                              (kb | k) != 0 ? 1u : 0u);
                     }
-                    umma_commit_pair_mc(empty(s), 0x3);  // frees slot s in both CTAs
+                    umma_commit_pair_mc(empty(s), 0x3);  // frees stage s in both CTAs
                     if (++s == STAGES) { s = 0; ph ^= 1u; }
                 }
                 if (!ok) break;
-                umma_commit_pair_mc(tfull(acc), 0x3);
+                umma_commit_pair_mc(tfull, 0x3);
             }
             // All pair MMAs issued by this thread complete before TMEM is released.
             umma_commit_pair(drain);
@@ -1044,12 +1108,14 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
         // ------------------------------- transform --------------------------------
         // Group g (4 warps, one thread per row of this CTA's A tile) converts the
         // K-steps kb with kb % G == g.  A warp covers 32 consecutive rows, which keeps
-        // the 64B-swizzled reads and the 128B-swizzled writes conflict-free.
+        // the 64B-swizzled code reads conflict-free and matches the tensor-memory
+        // lanes the warp may write (warp % 4 = lanes 32 (warp % 4) ..).
         const int t = threadIdx.x - 32 * kFirstTransformWarp;
         const int r = t & (BM - 1);
         const int grp = t / BM;
         const int groups = (p.num_kb + 7) / 8;  // 8 k-steps per scale group
-        const uint32_t fa16_base = mapa_shared(full_a16(0), 0);
+        const uint32_t full_base = mapa_shared(full(0), 0);
+        const uint32_t a_tmem_row = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + kTmemACol;
         bool ok = true;
         int tile = cluster;
         int m0 = 0, n0 = 0;
@@ -1059,8 +1125,6 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                      tile < num_tiles && grow < p.M);
         const uint32_t a8_row_off = (uint32_t)r * 64u;
         const uint32_t a8_xor = (uint32_t)((r >> 1) & 3);
-        const uint32_t a16_row_off = (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
-        const uint32_t a16_xor = (uint32_t)(r & 7);
         int64_t base_stage = 0;  // global stage index of kb = 0 of the current tile
         for (; ok && tile < num_tiles; tile += nclusters, base_stage += p.num_kb) {
             tile_coords(p, tile, m0, n0);
@@ -1086,7 +1150,7 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const uint32_t ph = (uint32_t)((i / STAGES) & 1);
                     const int j8 = (int)(i % A8_STAGES);
                     const uint32_t ph8 = (uint32_t)((i / A8_STAGES) & 1);
-                    // The BF16 slot is free once the MMAs of its previous round completed.
+                    // The A stage is free once the MMAs of its previous round completed.
                     // Waiting on it first also keeps every group within STAGES (<=
                     // A8_STAGES) stages of the MMA, so no parity wait below can match a
                     // phase one round too old.
@@ -1095,31 +1159,44 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                         ok = false;
                         break;
                     }
+                    tc_fence_after();  // the MMAs' reads of the stage come before the stores below
                     const uint8_t* a8 = smem + OFF_A8 + j8 * A8_BYTES;
                     uint4 q[4];
 #pragma unroll
                     for (int c = 0; c < 4; ++c)
                         q[c] = *reinterpret_cast<const uint4*>(a8 + a8_row_off + ((((uint32_t)c) ^ a8_xor) << 4));
                     const uint32_t sc2 = (uint32_t)(((j < 4) ? sc_lo : sc_hi) >> (16 * (j & 3))) & 0xFFFFu;
-                    uint8_t* a16 = smem + OFF_A16 + s * A16_BYTES + a16_row_off;
                     const uint32_t s0 = sc2 & 0xFFu, s1 = sc2 >> 8;
                     const int kvalid = p.K - kb * BK;
-                    if (!transform_row_fast(q, s0, s1, a16, a16_xor, kvalid))
-                        transform_row_exact(a8 + a8_row_off, a8_xor, s0, s1, a16, a16_xor, kvalid);
+                    const uint32_t ta = a_tmem_row + (uint32_t)s * kTmemAStageCols;
+                    // tcgen05.st is warp-collective: the warp takes one path together.
+                    if (__all_sync(0xFFFFFFFFu, fast_row_ok(q, s0, s1, kvalid))) {
+                        uint32_t out0[16], out1[16];
+                        convert_half_fast(q[0], q[1], s0, out0);
+                        tmem_st_32x32b_x16(ta, out0);
+                        convert_half_fast(q[2], q[3], s1, out1);
+                        tmem_st_32x32b_x16(ta + 16u, out1);
+                    } else {
+                        uint32_t ex[32];
+                        convert_row_exact(a8 + a8_row_off, a8_xor, s0, s1, kvalid, ex);
+                        tmem_st_32x32b_x16(ta, ex);
+                        tmem_st_32x32b_x16(ta + 16u, ex + 16);
+                    }
                     // The codes are consumed: release the A-code slot to the producer.
                     __syncwarp();
                     if (lane == 0) mbar_arrive(a8_empty(j8));
-                    fence_proxy_async_smem();
+                    tmem_st_wait();
+                    tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive_cluster(fa16_base + 8u * s);
+                    if (lane == 0) mbar_arrive_cluster(full_base + 8u * s);
                 }
             }
         }
     } else {
         setmaxnreg_inc<kEpiRegs>();
         // -------------------------------- epilogue --------------------------------
-        run_epilogue<false, false>(p, tmem_base, tfull(0), mapa_shared(tempty(0), 0), cluster, nclusters, rank,
-                                   warp, lane, abort_flag);
+        run_epilogue_onchip(p, tmem_base, tfull, mapa_shared(tempty, 0), cluster, nclusters, rank, warp, lane,
+                            abort_flag);
     }
 
     // ------------------------------- teardown -------------------------------------
