@@ -452,18 +452,21 @@ __device__ __noinline__ void sk_store_partial(float4* slot_row, uint32_t tacc, b
 }
 
 // 16 scale bytes of one row starting at block index b0 (bytes past the row end
-// or of an out-of-range row read as 0).  Issued one group of 8 k-steps ahead.
+// or of an out-of-range row read as 0).  Issued one group of 8 k-steps ahead: with
+// `vec` (the row's scale bytes are 16-byte aligned and a whole number of groups
+// long) one 16-byte load whose result is first used a group later, so its latency
+// overlaps the conversion of the current group; otherwise byte loads.
 __device__ __forceinline__ uint4 load_scale_group(const uint8_t* __restrict__ row_scales, int b0,
-                                                  int nblk, bool row_ok)
+                                                  int nblk, bool row_ok, bool vec)
 {
+    if (!row_ok) return make_uint4(0u, 0u, 0u, 0u);
+    if (vec) return __ldg(reinterpret_cast<const uint4*>(row_scales + b0));
     uint32_t w[4] = {0u, 0u, 0u, 0u};
-    if (row_ok) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const int b = b0 + i;
-            const uint32_t v = (b < nblk) ? (uint32_t)__ldg(row_scales + b) : 0u;
-            w[i >> 2] |= v << (8 * (i & 3));
-        }
+    for (int i = 0; i < 16; ++i) {
+        const int b = b0 + i;
+        const uint32_t v = (b < nblk) ? (uint32_t)__ldg(row_scales + b) : 0u;
+        w[i >> 2] |= v << (8 * (i & 3));
     }
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
@@ -1121,8 +1124,9 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
         int m0 = 0, n0 = 0;
         if (tile < num_tiles) tile_coords(p, tile, m0, n0);
         int grow = m0 + BM * (int)rank + r;
+        const bool sc_vec = p.nblkK % 16 == 0 && (reinterpret_cast<uintptr_t>(p.A_scales) & 15u) == 0;
         uint4 nxt = load_scale_group(p.A_scales + (int64_t)grow * p.nblkK, 0, p.nblkK,
-                                     tile < num_tiles && grow < p.M);
+                                     tile < num_tiles && grow < p.M, sc_vec);
         const uint32_t a8_row_off = (uint32_t)r * 64u;
         const uint32_t a8_xor = (uint32_t)((r >> 1) & 3);
         int64_t base_stage = 0;  // global stage index of kb = 0 of the current tile
@@ -1137,7 +1141,7 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     if (nt < num_tiles) tile_coords(p, nt, nm0, nn0);
                     const int nrow = nm0 + BM * (int)rank + r;
                     nxt = load_scale_group(p.A_scales + (int64_t)nrow * p.nblkK, 16 * ng, p.nblkK,
-                                           nt < num_tiles && nrow < p.M);
+                                           nt < num_tiles && nrow < p.M, sc_vec);
                 }
                 const uint64_t sc_lo = ((uint64_t)cur.y << 32) | cur.x;  // k-steps 0..3 of the group
                 const uint64_t sc_hi = ((uint64_t)cur.w << 32) | cur.z;  // k-steps 4..7

@@ -98,6 +98,32 @@ def test_ws_exotic_scales_and_nan_codes(mpk_lib, cuda, with_nan):
     assert hist[0] + hist[1] >= 0.999 * sum(hist)
 
 
+@pytest.mark.parametrize("M,N,K,offset", [(512, 512, 2048, 1), (512, 512, 2048, 0), (384, 256, 1600, 0),
+                                          (256, 512, 4096, 8)])
+def test_onchip_scale_byte_placement(whole_tiles, cuda, M, N, K, offset):
+    """The on-chip kernel reads each row's A scale bytes 16 at a time when they are
+    16-byte aligned and K is a multiple of 512, else byte by byte: scales at an odd
+    or 8-byte offset and a K that is not a multiple of 512 give the same D as the
+    pre-pass path."""
+    import torch
+
+    mpk_lib = whole_tiles
+    inp = O.make_gemm_inputs(M, N, K, seed=M + K + offset)
+    want_d, want_s = run_gemm(mpk_lib, inp)
+    A, B = to_dev(inp["A_data"]), to_dev(inp["B_bf16"])
+    C, Cs = to_dev(inp["C_data"]), to_dev(inp["C_scales"])
+    sc = inp["A_scales"]
+    buf = torch.zeros((sc.size + 64,), dtype=torch.uint8, device="cuda")
+    As = buf[offset:offset + sc.size].view(sc.shape)
+    As.copy_(to_dev(sc))
+    D = torch.full((M, N), 0xEE, dtype=torch.uint8, device="cuda")
+    Ds = torch.full((M, N // 32), 0xEE, dtype=torch.uint8, device="cuda")
+    mpk_lib.gemm_fp8_tensorcore_ws(A, As, B, C, Cs, D, Ds, M, N, K, None)
+    torch.cuda.synchronize()
+    assert np.array_equal(to_host(D), want_d) and np.array_equal(to_host(Ds), want_s)
+    assert mpk_lib.device_status() == 0
+
+
 def test_ws_prepass_is_exact_bf16(mpk_lib, cuda):
     """The workspace holds code x 2^(s-127) rounded to BF16 (exact for s >= 3)."""
     import torch
