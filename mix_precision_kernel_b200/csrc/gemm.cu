@@ -526,7 +526,12 @@ __device__ __noinline__ void convert_row_exact(const uint8_t* a8row, uint32_t a8
 // Each code's sign and 7 magnitude bits are moved into a BF16 bit pattern equal to
 // code x 2^-120 (the E4M3 exponent bits land in the low BF16 exponent bits; E4M3
 // subnormals become BF16 subnormals); one BF16 multiply by 2^(s-7) -- a power of
-// two, so exact -- gives code x 2^(s-127).  Integer ops and mul.rn.bf16x2 only.
+// two, so exact -- gives code x 2^(s-127).  Integer ops and mul.rn.bf16x2 only:
+// per pair of codes one prmt puts each code byte in the low byte of a 16-bit lane
+// with its sign bit replicated through the high byte, a shift by 4 moves the 7
+// magnitude bits to bits 4..10 (the sign copies to bits 11..15, and the low lane's
+// top nibble into the high lane's bits 0..3), and the mask 0x87F0 per lane keeps
+// the magnitude and bit 15.
 __device__ __forceinline__ bool fast_row_ok(const uint4 (&q)[4], uint32_t s0, uint32_t s1, int kvalid)
 {
     uint32_t nan_probe = 0u;
@@ -546,11 +551,10 @@ __device__ __forceinline__ void convert_half_fast(uint4 qa, uint4 qb, uint32_t s
     const uint32_t in[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
-        const uint32_t wm = in[w] & 0x7F7F7F7Fu, ws = in[w] & 0x80808080u;
-        const uint32_t m01 = prmt(wm, 0u, 0x4140u), s01 = prmt(ws, 0u, 0x1404u);
-        const uint32_t m23 = prmt(wm, 0u, 0x4342u), s23 = prmt(ws, 0u, 0x3424u);
-        out[2 * w] = mul_bf16x2(m01 * 16u + s01, f);
-        out[2 * w + 1] = mul_bf16x2(m23 * 16u + s23, f);
+        const uint32_t b01 = prmt(in[w], 0u, 0x9180u);  // codes 0, 1: byte, sign fill
+        const uint32_t b23 = prmt(in[w], 0u, 0xB3A2u);  // codes 2, 3
+        out[2 * w] = mul_bf16x2((b01 << 4) & 0x87F087F0u, f);
+        out[2 * w + 1] = mul_bf16x2((b23 << 4) & 0x87F087F0u, f);
     }
 }
 
@@ -891,12 +895,41 @@ __device__ __forceinline__ void run_epilogue_onchip(const Params& p, uint32_t tm
         }
         if (!mbar_wait(tfull, (uint32_t)it & 1u, abort_flag, p.status, kSiteTmemFull, p.timeout_ns)) break;
         tc_fence_after();
+        const uint32_t trow = tmem_base + ((uint32_t)(quad * 32) << 16);
+        if (p.vec_cd && n0 + BN <= p.N) {
+            // Whole tile inside N: two chunks per tensor-memory load, and the
+            // accumulator is released as soon as the last two chunks are in registers,
+            // so the next tile's MMAs start while their math and stores run.
+#pragma unroll
+            for (int pr = 0; pr < BN / 64; ++pr) {
+                uint32_t raw[64];
+                tmem_ld_32x32b_x64(trow + (uint32_t)(64 * pr), raw);
+                tmem_ld_wait();
+                if (pr == BN / 64 - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(tempty_rank0);
+                }
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int c = 2 * pr + h;
+                    float v[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[32 * h + i]);
+                    if (has_c) add_c_chunk(v, cq[c][0], cq[c][1], cs[c]);
+                    uint4 d0, d1;
+                    const uint32_t sd = quantize_block32(v, d0, d1);
+                    if (row_ok) store_d_chunk<false>(p, grow, n0 + 32 * c, d0, d1, sd);
+                }
+            }
+            continue;
+        }
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) {
             if (c >= nchunks) break;  // warp-uniform: tcgen05.ld is warp-collective
             const int col0 = n0 + 32 * c;
             const int valid = min(32, p.N - col0);
-            const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(32 * c);
+            const uint32_t taddr = trow + (uint32_t)(32 * c);
             if (valid == 32 && p.vec_cd) {
                 uint32_t raw[32];
                 tmem_ld_32x32b_x32(taddr, raw);
