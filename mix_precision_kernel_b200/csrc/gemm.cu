@@ -75,16 +75,20 @@ constexpr int kMaxGatherDest = 8;      // destinations of the fused all-gather (
 constexpr int BN = 256;        // output columns per tile (each CTA loads BN/2 of B)
 constexpr int BN_HALF = BN / 2;
 constexpr int BK = 64;
+// On-chip variant: a stage is a K block of OC_BK = 2 K-steps (one barrier wait and
+// one commit per 8 MMAs); ring of STAGES blocks consumed by the MMA (B halves in
+// shared memory and the converted BF16 A tile in tensor memory per stage) and ring
+// of A8_STAGES A-code blocks consumed by the transform.
+constexpr int OC_KSTEPS = 2;
+constexpr int OC_BK = OC_KSTEPS * 64;
 #ifndef MPK_STAGES
-#define MPK_STAGES 8
+#define MPK_STAGES 4
 #endif
-// On-chip variant: ring of K-steps consumed by the MMA (a B half in shared memory and
-// the converted BF16 A tile in tensor memory per stage).
 constexpr int STAGES = MPK_STAGES;
 #ifndef MPK_A8_STAGES
-#define MPK_A8_STAGES 8
+#define MPK_A8_STAGES 4
 #endif
-constexpr int A8_STAGES = MPK_A8_STAGES;  // ring of A code tiles (consumed by the transform)
+constexpr int A8_STAGES = MPK_A8_STAGES;
 constexpr int UMMA_K = 16;
 
 #ifndef MPK_TRANSFORM_GROUPS
@@ -125,24 +129,25 @@ static_assert(128 * kCtrlRegs + 32 * kTransformWarps * kXformRegs + 128 * kEpiRe
 #endif
 constexpr int kCPrefetch = MPK_C_PREFETCH;  // C chunks (32 columns) prefetched per round
 
-constexpr int A8_BYTES = BM * BK;               // 8192
+constexpr int A8_BYTES = BM * OC_BK;            // on-chip A codes per CTA and stage: 16384
 constexpr int A16_BYTES = BM * BK * 2;          // 16384
 constexpr int B_BOX_BYTES = 64 * BK * 2;        // one 64(N) x 64(K) box: 8192
 constexpr int B_BYTES = BK * BN_HALF * 2;       // 16384 per CTA
 constexpr uint32_t kTmemCols = 2 * BN;          // all 512 columns of tensor memory
 
 // On-chip variant's tensor memory (per CTA, 128 lanes = the CTA's 128 tile rows):
-// one FP32 accumulator of BN columns, then the BF16 A ring: one stage per K-step,
-// 32 columns (64 BF16 of a row, two per 32-bit column).  Pair MMAs of N = 128 (two
+// one FP32 accumulator of BN columns, then the BF16 A ring: one stage per K block,
+// 64 columns (128 BF16 of a row, two per 32-bit column).  Pair MMAs of N = 128 (two
 // per K slice into two half accumulators) run at about two thirds of the rate of
 // N = 256 on B200, so the tile keeps one N = 256 accumulator and the epilogue's
 // drain is not overlapped with the next tile's MMAs.
 constexpr uint32_t kTmemACol = BN;
-constexpr uint32_t kTmemAStageCols = BK / 2;
+constexpr uint32_t kTmemAStageCols = OC_BK / 2;
 static_assert(kTmemACol + STAGES * kTmemAStageCols <= kTmemCols, "tensor memory holds 512 columns");
 
+constexpr int OC_B_BYTES = OC_KSTEPS * B_BYTES;  // on-chip B per CTA and stage: 32768
 constexpr int OFF_B = 0;
-constexpr int OFF_A8 = OFF_B + STAGES * B_BYTES;
+constexpr int OFF_A8 = OFF_B + STAGES * OC_B_BYTES;
 constexpr int OFF_BAR = OFF_A8 + A8_STAGES * A8_BYTES;
 // barriers: a8_full[S8], a8_empty[S8], full[S], empty[S], tfull, tempty, drain
 constexpr int kNumBars = 2 * A8_STAGES + 2 * STAGES + 3;
@@ -169,6 +174,7 @@ struct Params {
     int M, N, K;
     int nblkK, nblkN;
     int num_m_tiles, num_n_tiles, num_kb;
+    int num_kb2;  // on-chip kernel: K blocks of OC_BK (two K-steps)
     // Work items (item_coords): items below split_from are whole tiles in raster
     // order; the remaining raster tiles are each cut into two 256 x 128 items.
     int num_items, split_from;
@@ -485,24 +491,25 @@ __device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b)
     return d;
 }
 
-// One row of one K-step of the on-chip variant: 64 E4M3 codes with the E8M0 scale
-// bytes s0 (codes 0..31) and s1 (codes 32..63) -> 64 BF16, packed two per 32-bit
-// word in K order (word j = codes 2j, 2j+1, the lower one in the low half), which is
-// the row's layout in a tensor-memory A operand (lane = row, 32-bit column j).
+// One row of one K block of the on-chip variant: 128 E4M3 codes (eight 16-code
+// chunks) with four E8M0 scale bytes packed in `scales` (byte q for codes
+// 32q .. 32q+31) -> 128 BF16, packed two per 32-bit word in K order (word j = codes
+// 2j, 2j+1, the lower one in the low half), which is the row's layout in a
+// tensor-memory A operand (lane = row, 32-bit column j).
 //
 // Exact general path: E4M3 -> f16 -> f32 with hardware conversions, multiply by
 // the FP32 scale (byte 0 -> 0.0 and 255 -> inf, as in the reference), round to
 // BF16; codes at K offset >= kvalid become zeros.  Used for scale bytes outside
 // 3..134, NaN codes and the K tail; kept out of line so the hot loop stays small.
-__device__ __noinline__ void convert_row_exact(const uint8_t* a8row, uint32_t a8xr, uint32_t s0, uint32_t s1,
-                                               int kvalid, uint32_t* out)
+__device__ __noinline__ void convert_block_exact(const uint8_t* a8row, uint32_t a8xr, uint32_t scales, int kvalid,
+                                                 uint32_t* out)
 {
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-        // Chunk c (codes 16c .. 16c+15), re-read from the 64-byte swizzled code row.
+    for (int c = 0; c < OC_BK / 16; ++c) {
+        // Chunk c (codes 16c .. 16c+15), re-read from the 128-byte swizzled code row.
         const uint4 qc = *reinterpret_cast<const uint4*>(a8row + ((((uint32_t)c) ^ a8xr) << 4));
         const uint32_t in[4] = {qc.x, qc.y, qc.z, qc.w};
-        const float scale = e8m0_to_f32(c < 2 ? s0 : s1);
+        const float scale = e8m0_to_f32((scales >> (8 * (c / 2))) & 0xFFu);
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
 #pragma unroll
@@ -519,10 +526,11 @@ __device__ __noinline__ void convert_row_exact(const uint8_t* a8row, uint32_t a8
     }
 }
 
-// Fast path for one row of one K-step (same contract as convert_row_exact), valid
-// when both scale bytes are in 3..134, no code is NaN (0x7F/0xFF) and all 64 codes
-// are inside K: fast_row_ok checks this on the four 16-code chunks q[0..3], and
-// convert_half_fast converts 32 codes (two chunks, one scale byte s) to 16 words.
+// Fast path for one row of one K block (same contract as convert_block_exact),
+// valid when all four scale bytes are in 3..134, no code is NaN (0x7F/0xFF) and all
+// 128 codes are inside K: fast_block_ok checks this on the eight 16-code chunks
+// q[0..7], and convert_half_fast converts 32 codes (two chunks, one scale byte s)
+// to 16 words.
 // Each code's sign and 7 magnitude bits are moved into a BF16 bit pattern equal to
 // code x 2^-120 (the E4M3 exponent bits land in the low BF16 exponent bits; E4M3
 // subnormals become BF16 subnormals); one BF16 multiply by 2^(s-7) -- a power of
@@ -532,16 +540,19 @@ __device__ __noinline__ void convert_row_exact(const uint8_t* a8row, uint32_t a8
 // magnitude bits to bits 4..10 (the sign copies to bits 11..15, and the low lane's
 // top nibble into the high lane's bits 0..3), and the mask 0x87F0 per lane keeps
 // the magnitude and bit 15.
-__device__ __forceinline__ bool fast_row_ok(const uint4 (&q)[4], uint32_t s0, uint32_t s1, int kvalid)
+__device__ __forceinline__ bool fast_block_ok(const uint4 (&q)[OC_BK / 16], uint32_t scales, int kvalid)
 {
     uint32_t nan_probe = 0u;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < OC_BK / 16; ++c) {
         const uint32_t in[4] = {q[c].x, q[c].y, q[c].z, q[c].w};
 #pragma unroll
         for (int w = 0; w < 4; ++w) nan_probe |= (in[w] & 0x7F7F7F7Fu) + 0x01010101u;  // 0x7F -> 0x80
     }
-    return (s0 - 3u) <= 131u && (s1 - 3u) <= 131u && (nan_probe & 0x80808080u) == 0u && kvalid >= 64;
+    bool ok = (nan_probe & 0x80808080u) == 0u && kvalid >= OC_BK;
+#pragma unroll
+    for (int b = 0; b < OC_BK / 32; ++b) ok = ok && (((scales >> (8 * b)) & 0xFFu) - 3u) <= 131u;
+    return ok;
 }
 
 __device__ __forceinline__ void convert_half_fast(uint4 qa, uint4 qb, uint32_t s, uint32_t (&out)[16])
@@ -1034,18 +1045,21 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
             for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
                 int m0, n0;
                 tile_coords(p, tile, m0, n0);
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb2 = 0; kb2 < p.num_kb2; ++kb2) {
                     if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, p.status, kSiteEmpty, p.timeout_ns)) {
                         ok = false;
                         break;
                     }
-                    // B boxes of both CTAs complete on rank 0's full.
-                    if (rank == 0) mbar_arrive_expect_tx(full(s), 2 * B_BYTES);
+                    // B boxes of both CTAs complete on rank 0's full: per K-step h of the
+                    // block, this CTA's two 64-column boxes (rows past K read as zeros).
+                    if (rank == 0) mbar_arrive_expect_tx(full(s), 2 * OC_B_BYTES);
                     const uint32_t fb = mapa_shared(full(s), 0);
 #pragma unroll
-                    for (int j = 0; j < BN_HALF / 64; ++j)
-                        tma_load_2d_pair(sbase + OFF_B + s * B_BYTES + j * B_BOX_BYTES, &tmap_b, fb,
-                                         n0 + BN_HALF * (int)rank + 64 * j, kb * BK);
+                    for (int h = 0; h < OC_KSTEPS; ++h)
+#pragma unroll
+                        for (int j = 0; j < BN_HALF / 64; ++j)
+                            tma_load_2d_pair(sbase + OFF_B + s * OC_B_BYTES + h * B_BYTES + j * B_BOX_BYTES, &tmap_b,
+                                             fb, n0 + BN_HALF * (int)rank + 64 * j, (kb2 * OC_KSTEPS + h) * BK);
                     ++issued;
                     if (++s == STAGES) { s = 0; ph ^= 1u; }
                 }
@@ -1074,13 +1088,13 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 int m0, n0;
                 tile_coords(p, tile, m0, n0);
                 const int row0 = m0 + BM * (int)rank;
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb2 = 0; kb2 < p.num_kb2; ++kb2) {
                     if (!mbar_wait(a8_empty(j), ph ^ 1u, abort_flag, p.status, kSiteEmptyA8, p.timeout_ns)) {
                         ok = false;
                         break;
                     }
                     mbar_arrive_expect_tx(a8_full(j), A8_BYTES);
-                    tma_load_2d(sbase + OFF_A8 + j * A8_BYTES, &tmap_a, a8_full(j), kb * BK, row0);
+                    tma_load_2d(sbase + OFF_A8 + j * A8_BYTES, &tmap_a, a8_full(j), kb2 * OC_BK, row0);
                     ++issued;
                     if (++j == A8_STAGES) { j = 0; ph ^= 1u; }
                 }
@@ -1110,22 +1124,28 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     break;
                 }
                 tc_fence_after();
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb2 = 0; kb2 < p.num_kb2; ++kb2) {
                     if (!mbar_wait(full(s), ph, abort_flag, p.status, kSiteFullB, p.timeout_ns)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint32_t a_tmem = tmem_base + kTmemACol + (uint32_t)s * kTmemAStageCols;
-                    const uint32_t b_addr = sbase + OFF_B + s * B_BYTES;
+                    const uint32_t b_addr = sbase + OFF_B + s * OC_B_BYTES;
+                    // The block's second K-step lies past K when num_kb is odd: its MMAs
+                    // are not issued (they would add zeros).
+                    const int nslices = (kb2 * OC_KSTEPS + 1 < p.num_kb ? OC_KSTEPS : 1) * (BK / UMMA_K);
 #pragma unroll
-                    for (int k = 0; k < BK / UMMA_K; ++k) {
-                        // B: MN-major, 64-column chunks 8 KiB apart (LBO), 8-row K groups
-                        // 1024 B apart (SBO); a K step of 16 rows is 2 KiB.  A: a K step of
-                        // 16 BF16 is 8 tensor-memory columns.
-                        const uint64_t bdesc = umma_smem_desc_sw128(b_addr + k * UMMA_K * 128, B_BOX_BYTES, 1024);
+                    for (int k = 0; k < OC_KSTEPS * (BK / UMMA_K); ++k) {
+                        if (k >= nslices) break;
+                        // B: MN-major, per K-step two 64-column chunks 8 KiB apart (LBO),
+                        // 8-row K groups 1024 B apart (SBO); a K slice of 16 rows is 2 KiB.
+                        // A: a K slice of 16 BF16 is 8 tensor-memory columns.
+                        const uint64_t bdesc = umma_smem_desc_sw128(
+                            b_addr + (k / (BK / UMMA_K)) * B_BYTES + (k % (BK / UMMA_K)) * UMMA_K * 128, B_BOX_BYTES,
+                            1024);
                         umma_bf16_pair_tmem_a(tmem_base, a_tmem + (uint32_t)(k * UMMA_K / 2), bdesc, kIdesc,
-                                              (kb | k) != 0 ? 1u : 0u);
+                                              (kb2 | k) != 0 ? 1u : 0u);
                     }
                     umma_commit_pair_mc(empty(s), 0x3);  // frees stage s in both CTAs
                     if (++s == STAGES) { s = 0; ph ^= 1u; }
@@ -1143,13 +1163,15 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
         if constexpr (kXformRegs < kLaunchRegs) setmaxnreg_dec<kXformRegs>();
         // ------------------------------- transform --------------------------------
         // Group g (4 warps, one thread per row of this CTA's A tile) converts the
-        // K-steps kb with kb % G == g.  A warp covers 32 consecutive rows, which keeps
-        // the 64B-swizzled code reads conflict-free and matches the tensor-memory
-        // lanes the warp may write (warp % 4 = lanes 32 (warp % 4) ..).
+        // K blocks kb2 with kb2 % G == g.  A warp covers 32 consecutive rows, which
+        // keeps the 128B-swizzled code reads conflict-free and matches the
+        // tensor-memory lanes the warp may write (warp % 4 = lanes 32 (warp % 4) ..).
         const int t = threadIdx.x - 32 * kFirstTransformWarp;
         const int r = t & (BM - 1);
         const int grp = t / BM;
-        const int groups = (p.num_kb + 7) / 8;  // 8 k-steps per scale group
+        // A scale group is 16 scale bytes: 4 K blocks of a row.
+        constexpr int kBlocksPerGroup = 16 * 32 / OC_BK;
+        const int groups = (p.num_kb2 + kBlocksPerGroup - 1) / kBlocksPerGroup;
         const uint32_t full_base = mapa_shared(full(0), 0);
         const uint32_t a_tmem_row = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + kTmemACol;
         bool ok = true;
@@ -1160,10 +1182,10 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
         const bool sc_vec = p.nblkK % 16 == 0 && (reinterpret_cast<uintptr_t>(p.A_scales) & 15u) == 0;
         uint4 nxt = load_scale_group(p.A_scales + (int64_t)grow * p.nblkK, 0, p.nblkK,
                                      tile < num_tiles && grow < p.M, sc_vec);
-        const uint32_t a8_row_off = (uint32_t)r * 64u;
-        const uint32_t a8_xor = (uint32_t)((r >> 1) & 3);
-        int64_t base_stage = 0;  // global stage index of kb = 0 of the current tile
-        for (; ok && tile < num_tiles; tile += nclusters, base_stage += p.num_kb) {
+        const uint32_t a8_row_off = (uint32_t)r * (uint32_t)OC_BK;
+        const uint32_t a8_xor = (uint32_t)(r & 7);
+        int64_t base_stage = 0;  // global stage index of kb2 = 0 of the current tile
+        for (; ok && tile < num_tiles; tile += nclusters, base_stage += p.num_kb2) {
             tile_coords(p, tile, m0, n0);
             for (int g = 0; ok && g < groups; ++g) {
                 const uint4 cur = nxt;
@@ -1176,13 +1198,11 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     nxt = load_scale_group(p.A_scales + (int64_t)nrow * p.nblkK, 16 * ng, p.nblkK,
                                            nt < num_tiles && nrow < p.M, sc_vec);
                 }
-                const uint64_t sc_lo = ((uint64_t)cur.y << 32) | cur.x;  // k-steps 0..3 of the group
-                const uint64_t sc_hi = ((uint64_t)cur.w << 32) | cur.z;  // k-steps 4..7
 #pragma unroll 1
-                for (int j = grp; j < 8; j += kTransformGroups) {
-                    const int kb = g * 8 + j;
-                    if (kb >= p.num_kb) break;
-                    const int64_t i = base_stage + kb;  // global stage index
+                for (int j = grp; j < kBlocksPerGroup; j += kTransformGroups) {
+                    const int kb2 = g * kBlocksPerGroup + j;
+                    if (kb2 >= p.num_kb2) break;
+                    const int64_t i = base_stage + kb2;  // global stage index
                     const int s = (int)(i % STAGES);
                     const uint32_t ph = (uint32_t)((i / STAGES) & 1);
                     const int j8 = (int)(i % A8_STAGES);
@@ -1198,26 +1218,27 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     }
                     tc_fence_after();  // the MMAs' reads of the stage come before the stores below
                     const uint8_t* a8 = smem + OFF_A8 + j8 * A8_BYTES;
-                    uint4 q[4];
+                    uint4 q[OC_BK / 16];
 #pragma unroll
-                    for (int c = 0; c < 4; ++c)
+                    for (int c = 0; c < OC_BK / 16; ++c)
                         q[c] = *reinterpret_cast<const uint4*>(a8 + a8_row_off + ((((uint32_t)c) ^ a8_xor) << 4));
-                    const uint32_t sc2 = (uint32_t)(((j < 4) ? sc_lo : sc_hi) >> (16 * (j & 3))) & 0xFFFFu;
-                    const uint32_t s0 = sc2 & 0xFFu, s1 = sc2 >> 8;
-                    const int kvalid = p.K - kb * BK;
+                    // This block's 4 scale bytes: word j of the group.
+                    const uint32_t sc4 = j < 2 ? (j == 0 ? cur.x : cur.y) : (j == 2 ? cur.z : cur.w);
+                    const int kvalid = p.K - kb2 * OC_BK;
                     const uint32_t ta = a_tmem_row + (uint32_t)s * kTmemAStageCols;
                     // tcgen05.st is warp-collective: the warp takes one path together.
-                    if (__all_sync(0xFFFFFFFFu, fast_row_ok(q, s0, s1, kvalid))) {
-                        uint32_t out0[16], out1[16];
-                        convert_half_fast(q[0], q[1], s0, out0);
-                        tmem_st_32x32b_x16(ta, out0);
-                        convert_half_fast(q[2], q[3], s1, out1);
-                        tmem_st_32x32b_x16(ta + 16u, out1);
+                    if (__all_sync(0xFFFFFFFFu, fast_block_ok(q, sc4, kvalid))) {
+#pragma unroll
+                        for (int h = 0; h < OC_BK / 32; ++h) {
+                            uint32_t out[16];
+                            convert_half_fast(q[2 * h], q[2 * h + 1], (sc4 >> (8 * h)) & 0xFFu, out);
+                            tmem_st_32x32b_x16(ta + 16u * (uint32_t)h, out);
+                        }
                     } else {
-                        uint32_t ex[32];
-                        convert_row_exact(a8 + a8_row_off, a8_xor, s0, s1, kvalid, ex);
-                        tmem_st_32x32b_x16(ta, ex);
-                        tmem_st_32x32b_x16(ta + 16u, ex + 16);
+                        uint32_t ex[OC_BK / 2];
+                        convert_block_exact(a8 + a8_row_off, a8_xor, sc4, kvalid, ex);
+#pragma unroll
+                        for (int h = 0; h < OC_BK / 32; ++h) tmem_st_32x32b_x16(ta + 16u * (uint32_t)h, ex + 16 * h);
                     }
                     // The codes are consumed: release the A-code slot to the producer.
                     __syncwarp();
@@ -1676,6 +1697,7 @@ int gemm_setup(const uint8_t* A_scales, const void* B, int ldb, const uint8_t* C
     p.num_m_tiles = (M + PAIR_M - 1) / PAIR_M;
     p.num_n_tiles = (N + BN - 1) / BN;
     p.num_kb = (K + BK - 1) / BK;
+    p.num_kb2 = (p.num_kb + OC_KSTEPS - 1) / OC_KSTEPS;
     p.num_items = p.split_from = p.num_m_tiles * p.num_n_tiles;
     // About sqrt(74 clusters) rows per panel keeps the in-flight rectangle square;
     // up to 2 * kPanelM M tiles stay one panel (M fastest over all rows), which
@@ -1875,7 +1897,7 @@ int launch_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const
     int rc = gemm_setup(A_scales, B, N, C_data, C_scales, D_data, D_scales, M, N, K, dev, enc, tmap_b, p);
     if (rc) return rc;
     if ((rc = encode_2d(enc, &tmap_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, A_data, (uint64_t)K, (uint64_t)M,
-                        (uint64_t)K, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
+                        (uint64_t)K, OC_BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
     if ((rc = ensure_smem_attr((const void*)gemm_mxfp8_bf16_kernel, SMEM_BYTES, &g_smem_attr_set[dev])))
         return rc;
