@@ -59,7 +59,13 @@ enum {
  * free nodes.  If no workspace can be had, the kernel that converts A on chip runs
  * instead: it needs no workspace and gives a bit-identical D, but needs K % 16 == 0,
  * N % 8 == 0 and 16-byte aligned A_data and B (else MPK_ERR_UNSUPPORTED /
- * MPK_ERR_MISALIGNED). */
+ * MPK_ERR_MISALIGNED).
+ *
+ * Tall products with few columns -- N <= 2048 and M * K * 2 >= 256 MiB, under the
+ * default schedule, when the plan has no stream-K split and the operands meet the
+ * on-chip kernel's limits above -- take the on-chip kernel directly: there the extra
+ * pass of the pre-pass over A in HBM costs more than converting A inside the GEMM,
+ * and D is the same bit for bit.  mpk_gemm_path reports which path a call takes. */
 int mpk_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const void* B_bf16,
                         const uint8_t* C_data, const uint8_t* C_scales, uint8_t* D_data,
                         uint8_t* D_scales, int M, int N, int K, void* stream);
@@ -112,6 +118,16 @@ int mpk_gemm_schedule(void);
  * whole tiles; *tiles is the total number of 256x256 tiles.  No counterpart in the
  * reference. */
 int mpk_gemm_plan(int M, int N, int K, int* tiles, int* stream_k_tiles, int* stream_k_pairs);
+
+/* Kernel path of mpk_gemm_mxfp8_bf16 for these operands (*path):
+ *   MPK_PATH_PREPASS  A dequantized to BF16 by the pre-pass, then the BF16-A tensor-core
+ *                     kernel (two launches; falls back to MPK_PATH_ONCHIP only when
+ *                     no workspace can be had);
+ *   MPK_PATH_ONCHIP   the kernel that converts A on chip (one launch, no workspace).
+ * Depends on the shape, on A_data's and B's alignment and on the current schedule.
+ * No counterpart in the reference. */
+enum { MPK_PATH_PREPASS = 0, MPK_PATH_ONCHIP = 1 };
+int mpk_gemm_path(const void* A_data, const void* B_bf16, int M, int N, int K, int* path);
 
 /* Returns the current device's pooled GEMM workspace to the driver, once the
  * work queued on it has finished.  No counterpart in the reference. */

@@ -33,6 +33,7 @@ __all__ = [
     "gemm_fp8_tensorcore_noalloc", "NOALLOC_SCRATCH_BYTES",
     "gemm", "quantize", "dequantize", "device_status", "set_wait_timeout_ns", "wait_selftest",
     "set_gemm_schedule", "gemm_schedule", "gemm_plan", "SCHEDULE_AUTO", "SCHEDULE_TILES", "SCHEDULE_STREAM_K",
+    "gemm_path", "PATH_PREPASS", "PATH_ONCHIP",
     "MX_BLOCK", "nblk",
 ]
 
@@ -54,6 +55,9 @@ MPK_ERR_DRIVER = 1006
 SCHEDULE_AUTO = 0
 SCHEDULE_TILES = 1
 SCHEDULE_STREAM_K = 2
+# Kernel paths of the default GEMM entry point (MPK_PATH_* in include/mpk.h)
+PATH_PREPASS = 0
+PATH_ONCHIP = 1
 
 
 class MpkError(RuntimeError):
@@ -114,6 +118,7 @@ def lib() -> ctypes.CDLL:
             L.mpk_gemm_schedule.argtypes = []
             ip = ctypes.POINTER(ci)
             L.mpk_gemm_plan.argtypes = [ci, ci, ci, ip, ip, ip]
+            L.mpk_gemm_path.argtypes = [vp, vp, ci, ci, ci, ip]
             for f in ("mpk_gemm_mxfp8_bf16", "mpk_gemm_mxfp8_bf16_ws", "mpk_gemm_workspace_size",
                       "mpk_release_workspace_pool", "mpk_mxfp8_quantize", "mpk_mxfp8_dequantize",
                       "mpk_mxfp8_dequantize_bf16", "mpk_gemm_mxfp8_bf16_noalloc",
@@ -122,7 +127,7 @@ def lib() -> ctypes.CDLL:
                       "mpk_ipc_export", "mpk_ipc_import", "mpk_ipc_close",
                       "mpk_mxfp8_quantize_host", "mpk_mxfp8_dequantize_host", "mpk_device_status",
                       "mpk_set_wait_timeout_ns", "mpk_wait_selftest", "mpk_version",
-                      "mpk_set_gemm_schedule", "mpk_gemm_schedule", "mpk_gemm_plan"):
+                      "mpk_set_gemm_schedule", "mpk_gemm_schedule", "mpk_gemm_plan", "mpk_gemm_path"):
                 getattr(L, f).restype = ci
             _lib = L
     return _lib
@@ -353,6 +358,14 @@ def set_gemm_schedule(schedule: int) -> int:
 
 def gemm_schedule() -> int:
     return lib().mpk_gemm_schedule()
+
+
+def gemm_path(A_data, B, M: int, N: int, K: int) -> int:
+    """PATH_PREPASS or PATH_ONCHIP: the kernel path gemm_fp8_tensorcore takes for these
+    operands (tensors or device addresses) under the current schedule."""
+    path = ctypes.c_int(-1)
+    _check(lib().mpk_gemm_path(_addr(A_data), _addr(B), M, N, K, ctypes.byref(path)))
+    return path.value
 
 
 def gemm_plan(M: int, N: int, K: int) -> tuple[int, int, int]:

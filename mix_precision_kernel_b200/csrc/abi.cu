@@ -143,6 +143,17 @@ int mpk_gemm_plan(int M, int N, int K, int* tiles, int* stream_k_tiles, int* str
     return MPK_SUCCESS;
 }
 
+int mpk_gemm_path(const void* A_data, const void* B_bf16, int M, int N, int K, int* path)
+{
+    if (!path || M < 0 || N < 0 || K < 0) {
+        set_last_error("mpk_gemm_path: null output or negative size");
+        return MPK_ERR_INVALID_VALUE;
+    }
+    *path = K > 0 && M > 0 && N > 0 && gemm_default_onchip(A_data, B_bf16, M, N, K) ? MPK_PATH_ONCHIP
+                                                                                  : MPK_PATH_PREPASS;
+    return MPK_SUCCESS;
+}
+
 const char* mpk_status_string(int status)
 {
     switch (status) {
@@ -251,6 +262,11 @@ int mpk_gemm_mxfp8_bf16(const uint8_t* A_data, const uint8_t* A_scales, const vo
         return from_cuda(launch_mxfp8_requantize(C_data, C_scales, D_data, D_scales, M, N, st),
                          "requantize launch");
     }
+    // Tall products with few columns: the on-chip conversion kernel is faster than
+    // the pre-pass path and needs no workspace (gemm_default_onchip).
+    if (gemm_default_onchip(A_data, B_bf16, M, N, K))
+        return launch_gemm_mxfp8_bf16(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales, M, N,
+                                      K, st);
     // Pre-pass path.  Eager calls take the workspace from the library's pool on
     // `stream`.  While `stream` is being captured into a CUDA graph, the workspace
     // is a stream-ordered allocation of the device's default pool, which the

@@ -1871,6 +1871,24 @@ int check_onchip_gemm_shape(const uint8_t* A_data, const void* B, int N, int K)
     return MPK_SUCCESS;
 }
 
+// Default entry point: run the on-chip conversion kernel instead of the pre-pass and
+// the BF16-A kernel.  Measured on B200, the on-chip kernel is faster when N <= 2048
+// and the BF16 copy of A (M * K * 2 bytes) is at least 256 MiB, about twice L2:
+// the pre-pass then costs a whole extra pass over A in HBM (write 2 bytes, read 2
+// bytes back per code) against a GEMM with few columns to amortise it over.  Only
+// whole-tile plans (the default schedule with no stream-K split) are routed, so D
+// is the same bit for bit as the pre-pass path's; the operands must meet the
+// on-chip kernel's TMA limits.
+bool gemm_default_onchip(const void* A_data, const void* B, int M, int N, int K)
+{
+    using namespace gemm;
+    if (g_schedule.load(std::memory_order_relaxed) != MPK_SCHEDULE_AUTO) return false;
+    if (N > 2048 || (int64_t)M * K * 2 < (int64_t(256) << 20)) return false;
+    if (K % 16 != 0 || N % 8 != 0) return false;
+    if ((reinterpret_cast<uintptr_t>(A_data) & 15u) || (reinterpret_cast<uintptr_t>(B) & 15u)) return false;
+    return gemm_sk_plan(M, N, K).tiles == 0;
+}
+
 bool gemm_b_needs_copy(const void* B, int N)
 {
     return N % 8 != 0 || (reinterpret_cast<uintptr_t>(B) & 15u) != 0;

@@ -58,6 +58,9 @@ struct GatherDest {
     uint8_t* D_extra[7];
     uint8_t* Ds_extra[7];
 };
+// True when mpk_gemm_mxfp8_bf16 runs the on-chip conversion kernel for these
+// operands (tall products with few columns; see gemm.cu).
+bool gemm_default_onchip(const void* A_data, const void* B, int M, int N, int K);
 bool gemm_b_needs_copy(const void* B, int N);
 // 0 if `bytes` bytes at ptr lie in memory the current device may store to (an
 // allocation of this device, or a buffer imported on it with mpk_ipc_import).

@@ -27,7 +27,7 @@ def test_header_declares_the_reference_replacements():
     for n in ("mpk_gemm_mxfp8_bf16", "mpk_mxfp8_quantize", "mpk_mxfp8_dequantize",
               "mpk_mxfp8_quantize_host", "mpk_mxfp8_dequantize_host", "mpk_status_string",
               "mpk_last_error", "mpk_last_error_string", "mpk_device_status", "mpk_mxfp8_quantize_cols",
-              "mpk_mxfp8_quantize_bf16_cols", "mpk_set_gemm_schedule", "mpk_gemm_plan"):
+              "mpk_mxfp8_quantize_bf16_cols", "mpk_set_gemm_schedule", "mpk_gemm_plan", "mpk_gemm_path"):
         assert n in names, names
 
 
@@ -173,3 +173,31 @@ def test_collective_entry_points_validate_without_a_device(mpk_lib):
     out = ctypes.c_void_p(0)
     assert L.mpk_ipc_import(handle, 4096, 4096, ctypes.byref(out)) == MPK_ERR_INVALID_VALUE
     assert L.mpk_ipc_close(1 << 20) == MPK_ERR_INVALID_VALUE
+
+
+def test_default_path_routing(mpk_lib):
+    """mpk_gemm_mxfp8_bf16 sends tall products with few columns (N <= 2048 and a BF16
+    copy of A of at least 256 MiB) to the on-chip conversion kernel when the plan has
+    whole tiles only and the operands meet that kernel's TMA limits; everything else
+    takes the pre-pass path.  Host logic only (aligned fake addresses)."""
+    on, pre = mpk_lib.PATH_ONCHIP, mpk_lib.PATH_PREPASS
+    a, b = 1 << 20, 1 << 21  # 16-byte aligned addresses
+    path = lambda M, N, K, A=a, B=b: mpk_lib.gemm_path(A, B, M, N, K)
+    assert path(131072, 2048, 2048) == on      # the tall-skinny projection
+    assert path(262144, 512, 1024) == on
+    assert path(65536, 2048, 4096) == on
+    assert path(32768, 2048, 2048) == pre      # BF16 A of 128 MiB: fits L2 about once
+    assert path(131072, 4096, 2048) == pre     # more columns to amortise the pre-pass
+    assert path(4096, 12288, 4096) == pre
+    assert path(131072, 2048, 2056) == pre     # K % 16 != 0: TMA row stride
+    assert path(131072, 2044, 2048) == pre     # N % 8 != 0
+    assert path(131072, 2048, 2048, A=a + 8) == pre  # misaligned A codes
+    assert path(131072, 2048, 2048, B=b + 2) == pre  # misaligned B
+    assert path(0, 2048, 2048) == pre and path(131072, 2048, 0) == pre
+    prev = mpk_lib.set_gemm_schedule(mpk_lib.SCHEDULE_TILES)
+    try:
+        assert path(131072, 2048, 2048) == pre  # a forced schedule keeps the pre-pass kernel
+    finally:
+        mpk_lib.set_gemm_schedule(prev)
+    with pytest.raises(mpk_lib.MpkError):
+        mpk_lib.gemm_path(a, b, -1, 8, 16)

@@ -98,6 +98,34 @@ def test_ws_exotic_scales_and_nan_codes(mpk_lib, cuda, with_nan):
     assert hist[0] + hist[1] >= 0.999 * sum(hist)
 
 
+@pytest.mark.parametrize("M,N,K", [(131072, 2048, 2048), (65536, 1024, 4096), (262144, 512, 1024)])
+def test_default_path_takes_the_onchip_kernel_for_tall_products(mpk_lib, cuda, M, N, K):
+    """Tall products with few columns go straight to the on-chip conversion kernel
+    from the default entry point; D equals the pre-pass kernel's (caller workspace)
+    bit for bit, and the default call allocates no workspace."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    Ad, As = mpk_lib.quantize(torch.randn((M, K), generator=g, device="cuda") * 0.02)
+    Cd, Cs = mpk_lib.quantize(torch.randn((M, N), generator=g, device="cuda") * 0.02)
+    B = (torch.randn((K, N), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    assert mpk_lib.gemm_path(Ad, B, M, N, K) == mpk_lib.PATH_ONCHIP
+    D0 = torch.empty((M, N), dtype=torch.uint8, device="cuda")
+    S0 = torch.empty((M, N // 32), dtype=torch.uint8, device="cuda")
+    mpk_lib.release_workspace_pool()
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    mpk_lib.gemm_fp8_tensorcore(Ad, As, B, Cd, Cs, D0, S0, M, N, K)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] >= free0 - (2 << 20)  # no workspace reserved
+    D1, S1 = torch.empty_like(D0), torch.empty_like(S0)
+    ws = torch.empty((mpk_lib.gemm_workspace_size(M, N, K),), dtype=torch.uint8, device="cuda")
+    mpk_lib.gemm_fp8_tensorcore_ws(Ad, As, B, Cd, Cs, D1, S1, M, N, K, ws)
+    torch.cuda.synchronize()
+    assert torch.equal(D0, D1) and torch.equal(S0, S1)
+    assert mpk_lib.device_status() == 0
+
+
 @pytest.mark.parametrize("M,N,K,offset", [(512, 512, 2048, 1), (512, 512, 2048, 0), (384, 256, 1600, 0),
                                           (256, 512, 4096, 8)])
 def test_onchip_scale_byte_placement(whole_tiles, cuda, M, N, K, offset):
