@@ -136,7 +136,7 @@ int mpk_release_workspace_pool(void);
 /* Fixed size of the device array behind mpk_gemm_mxfp8_bf16_noalloc: 32 MiB per
  * device, enough for the BF16 copy of an A with M*K <= 16,777,216 (4096 x 4096) when
  * K % 8 == 0, N % 8 == 0 and B is 16-byte aligned (other shapes need the workspace
- * that mpk_gemm_mxfp8_bf16_ws describes). */
+ * that mpk_gemm_mxfp8_bf16_ws describes, or run on the on-chip conversion kernel). */
 #define MPK_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 
 /* Same computation as mpk_gemm_mxfp8_bf16, for callers that may not allocate
@@ -150,7 +150,11 @@ int mpk_release_workspace_pool(void);
  * stream capture (or run with CUDA_MODULE_LOADING=EAGER, which reserves it when the
  * context is created).  The array's address is looked up on every call, so calls
  * stay valid after cudaDeviceReset (whose next first call reserves it again).
- * Sizes whose workspace exceeds the array return MPK_ERR_UNSUPPORTED.  Nothing in
+ * Shapes the default entry point sends to the on-chip conversion kernel take it here
+ * too, and so do shapes whose workspace would exceed the array when K % 16 == 0,
+ * N % 8 == 0 and A_data and B are 16-byte aligned (that kernel needs no workspace;
+ * D is the whole-tile result); other sizes whose workspace exceeds the array return
+ * MPK_ERR_UNSUPPORTED.  Nothing in
  * the array needs to start at zero.  When the array also has room for the
  * stream-K partials (see mpk_set_gemm_schedule) the call uses them, otherwise it
  * runs whole tiles.  All calls on a device share the array: calls that can run at

@@ -688,11 +688,21 @@ extern "C" int mpk_gemm_mxfp8_bf16_noalloc(const uint8_t* A_data, const uint8_t*
     if (K == 0)
         return from_cuda(launch_mxfp8_requantize(C_data, C_scales, D_data, D_scales, M, N, st),
                          "requantize launch");
+    // The on-chip conversion kernel needs no workspace: it serves the shapes the
+    // default entry point routes to it, and any shape whose workspace would not fit
+    // the fixed scratch when the operands meet its limits.
+    if (gemm_default_onchip(A_data, B_bf16, M, N, K))
+        return launch_gemm_mxfp8_bf16(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales, M, N,
+                                      K, st);
     const size_t need = gemm_workspace_bytes_min(M, N, K, gemm_b_needs_copy(B_bf16, N));
     if (need > (size_t)MPK_NOALLOC_SCRATCH_BYTES) {
+        if (check_onchip_gemm_shape(A_data, B_bf16, N, K) == MPK_SUCCESS)
+            return launch_gemm_mxfp8_bf16(A_data, A_scales, B_bf16, C_data, C_scales, D_data, D_scales, M, N,
+                                          K, st);
         set_last_error("mpk_gemm_mxfp8_bf16_noalloc: the workspace of %zu bytes exceeds its fixed scratch "
-                       "of %zu bytes (M*K <= %zu for K %% 8 == 0, N %% 8 == 0 and 16-byte aligned B); use "
-                       "mpk_gemm_mxfp8_bf16 or mpk_gemm_mxfp8_bf16_ws",
+                       "of %zu bytes (M*K <= %zu for K %% 8 == 0, N %% 8 == 0 and 16-byte aligned B), and "
+                       "the on-chip conversion kernel needs K %% 16 == 0, N %% 8 == 0 and 16-byte aligned "
+                       "A_data and B; use mpk_gemm_mxfp8_bf16 or mpk_gemm_mxfp8_bf16_ws",
                        need, (size_t)MPK_NOALLOC_SCRATCH_BYTES, (size_t)MPK_NOALLOC_SCRATCH_BYTES / 2);
         return MPK_ERR_UNSUPPORTED;
     }

@@ -78,12 +78,13 @@ def test_largest_size_that_fits(mpk_lib, cuda):
 
 
 def test_oversize_is_rejected_before_any_launch(mpk_lib, cuda):
-    """M*K*2 above the fixed scratch returns MPK_ERR_UNSUPPORTED with a message
-    naming the limit, and leaves D untouched.  The buffers are real and full size,
-    so nothing could be read out of bounds even if a launch happened."""
+    """M*K*2 above the fixed scratch, with a K the on-chip kernel cannot take
+    (K % 16 != 0), returns MPK_ERR_UNSUPPORTED with a message naming the limit, and
+    leaves D untouched.  The buffers are real and full size, so nothing could be read
+    out of bounds even if a launch happened."""
     import torch
 
-    M, K, N = 4096, 4112, 64
+    M, K, N = 4096, 4104, 64
     assert M * K * 2 > mpk_lib.NOALLOC_SCRATCH_BYTES
     A = torch.zeros((M, K), dtype=torch.uint8, device="cuda")
     As = torch.full((M, (K + 31) // 32), 127, dtype=torch.uint8, device="cuda")
@@ -96,6 +97,30 @@ def test_oversize_is_rejected_before_any_launch(mpk_lib, cuda):
     assert "scratch" in str(e.value)
     torch.cuda.synchronize()
     assert bool((D == 0xEE).all()) and bool((Ds == 0xEE).all())
+    assert mpk_lib.device_status() == 0
+
+
+def test_oversize_runs_the_onchip_kernel(mpk_lib, cuda):
+    """A product whose BF16 A would not fit the scratch, within the on-chip kernel's
+    limits, runs on that kernel: D equals the default entry point's under whole
+    tiles, bit for bit, and no device memory is taken."""
+    import torch
+
+    M, N, K = 8192, 768, 4096  # BF16 A of 64 MiB
+    assert M * K * 2 > mpk_lib.NOALLOC_SCRATCH_BYTES
+    inp = O.make_gemm_inputs(M, N, K, seed=17)
+    prev = mpk_lib.set_gemm_schedule(mpk_lib.SCHEDULE_TILES)
+    try:
+        want_d, want_s = run_gemm(mpk_lib, inp)
+    finally:
+        mpk_lib.set_gemm_schedule(prev)
+    _noalloc(mpk_lib, inp)  # first call on the device loads the array
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    D, Ds = _noalloc(mpk_lib, inp)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] >= free0 - (2 << 20)
+    assert np.array_equal(to_host(D), want_d) and np.array_equal(to_host(Ds), want_s)
     assert mpk_lib.device_status() == 0
 
 
