@@ -1,5 +1,5 @@
 """Tensors with more than 2^31 elements: the library indexes with 64-bit
-arithmetic (the reference uses int).  Rows near the end of the
+arithmetic (the reference indexes with int).  Rows near the end of the
 tensors are checked against the oracle, which is exact for sampled rows (row i of
 D depends only on row i of A and C)."""
 import numpy as np
