@@ -964,11 +964,11 @@ __device__ __forceinline__ void run_epilogue_onchip(const Params& p, uint32_t tm
     }
 }
 
-// On-chip variant.  Per CTA and K-step: the TMA producer brings this CTA's 128 x 64
-// A codes (64-byte swizzle) and its half of the tile's B columns (two 64-column
-// boxes, tile columns 128 rank .. +127);
-// a transform group converts the codes to BF16 and stores them into the A stage in
-// tensor memory (tcgen05.st, lane = row); rank 0 issues the pair MMAs
+// On-chip variant.  Per CTA and K block of two K-steps: the A-code producer brings
+// this CTA's 128 x 128 A codes (128-byte swizzle), the B producer its half of the
+// tile's B columns for both K-steps (four 64 x 64 boxes, tile columns 128 rank ..
+// +127); a transform group converts the codes to BF16 and stores them into the A
+// stage in tensor memory (tcgen05.st, lane = row); rank 0 issues the pair MMAs
 // (tcgen05.mma.cta_group::2, A from tensor memory, B from shared memory, M = 256,
 // N = 256) into the accumulator.
 __global__ void __maxnreg__(kLaunchRegs)
