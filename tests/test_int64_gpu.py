@@ -12,7 +12,10 @@ from test_gemm_gpu import check_parity
 pytestmark = pytest.mark.gpu
 
 
-def test_gemm_d_beyond_2_31_elements(mpk_lib, cuda):
+@pytest.mark.parametrize("path", ["default", "onchip"])
+def test_gemm_d_beyond_2_31_elements(mpk_lib, cuda, path):
+    """Both GEMM kernels: the pre-pass path (the default entry point at this width)
+    and the on-chip conversion kernel (no workspace)."""
     import torch
 
     M, N, K = 65536, 36864, 64          # D: 2.4e9 elements
@@ -24,7 +27,12 @@ def test_gemm_d_beyond_2_31_elements(mpk_lib, cuda):
     C.normal_(0.0, 0.02, generator=g)
     Cd, Cs = mpk_lib.quantize(C)
     del C
-    D, Ds = mpk_lib.gemm(Ad, As, B, Cd, Cs)
+    if path == "default":
+        D, Ds = mpk_lib.gemm(Ad, As, B, Cd, Cs)
+    else:
+        D = torch.empty((M, N), dtype=torch.uint8, device="cuda")
+        Ds = torch.empty((M, N // 32), dtype=torch.uint8, device="cuda")
+        mpk_lib.gemm_fp8_tensorcore_ws(Ad, As, B, Cd, Cs, D, Ds, M, N, K, None)
     torch.cuda.synchronize()
     rows = np.array([0, 32767, 58254, M - 2, M - 1])
     A_h, As_h = to_host(Ad[rows]), to_host(As[rows])
@@ -33,7 +41,7 @@ def test_gemm_d_beyond_2_31_elements(mpk_lib, cuda):
     inp = {"M": len(rows), "N": N, "K": K, "A_data": A_h, "A_scales": As_h, "B_bf16": B_h,
            "C_data": C_h, "C_scales": Cs_h, "A_deq": O.dequantize(A_h, As_h),
            "B_f32": O.bf16_bits_to_float(B_h), "C_deq": O.dequantize(C_h, Cs_h)}
-    check_parity(to_host(D[rows]), to_host(Ds[rows]), O.gold_mx(inp), "D > 2^31 elements",
+    check_parity(to_host(D[rows]), to_host(Ds[rows]), O.gold_mx(inp), f"D > 2^31 elements ({path})",
                  ref_pass_mark=False)
     assert mpk_lib.device_status() == 0
 
