@@ -458,16 +458,24 @@ __device__ __noinline__ void sk_store_partial(float4* slot_row, uint32_t tacc, b
 }
 
 // 16 scale bytes of one row starting at block index b0 (bytes past the row end
-// or of an out-of-range row read as 0).  Issued one group of 8 k-steps ahead: with
-// `vec` (the row's scale bytes are 16-byte aligned and a whole number of groups
-// long) one 16-byte load whose result is first used a group later, so its latency
-// overlaps the conversion of the current group; otherwise byte loads.
+// or of an out-of-range row read as 0).  Issued one group of 8 k-steps ahead, the
+// result first used a group later, so the loads' latency overlaps the conversion
+// of the current group: `width` 16 (the row's scale bytes 16-byte aligned and a
+// whole number of groups long) one 16-byte load; 4 (4-byte aligned, a whole number
+// of 4-byte words) four word loads, words past the row end skipped; otherwise byte
+// loads packed on the spot (their latency exposed).
 __device__ __forceinline__ uint4 load_scale_group(const uint8_t* __restrict__ row_scales, int b0,
-                                                  int nblk, bool row_ok, bool vec)
+                                                  int nblk, bool row_ok, int width)
 {
     if (!row_ok) return make_uint4(0u, 0u, 0u, 0u);
-    if (vec) return __ldg(reinterpret_cast<const uint4*>(row_scales + b0));
+    if (width == 16) return __ldg(reinterpret_cast<const uint4*>(row_scales + b0));
     uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if (width == 4) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (b0 + 4 * i < nblk) w[i] = __ldg(reinterpret_cast<const uint32_t*>(row_scales + b0 + 4 * i));
+        return make_uint4(w[0], w[1], w[2], w[3]);
+    }
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
         const int b = b0 + i;
@@ -1179,9 +1187,11 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
         int m0 = 0, n0 = 0;
         if (tile < num_tiles) tile_coords(p, tile, m0, n0);
         int grow = m0 + BM * (int)rank + r;
-        const bool sc_vec = p.nblkK % 16 == 0 && (reinterpret_cast<uintptr_t>(p.A_scales) & 15u) == 0;
+        const int sc_width = p.nblkK % 16 == 0 && (reinterpret_cast<uintptr_t>(p.A_scales) & 15u) == 0 ? 16
+                             : p.nblkK % 4 == 0 && (reinterpret_cast<uintptr_t>(p.A_scales) & 3u) == 0 ? 4
+                                                                                                      : 1;
         uint4 nxt = load_scale_group(p.A_scales + (int64_t)grow * p.nblkK, 0, p.nblkK,
-                                     tile < num_tiles && grow < p.M, sc_vec);
+                                     tile < num_tiles && grow < p.M, sc_width);
         const uint32_t a8_row_off = (uint32_t)r * (uint32_t)OC_BK;
         const uint32_t a8_xor = (uint32_t)(r & 7);
         int64_t base_stage = 0;  // global stage index of kb2 = 0 of the current tile
@@ -1196,7 +1206,7 @@ gemm_mxfp8_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     if (nt < num_tiles) tile_coords(p, nt, nm0, nn0);
                     const int nrow = nm0 + BM * (int)rank + r;
                     nxt = load_scale_group(p.A_scales + (int64_t)nrow * p.nblkK, 16 * ng, p.nblkK,
-                                           nt < num_tiles && nrow < p.M, sc_vec);
+                                           nt < num_tiles && nrow < p.M, sc_width);
                 }
 #pragma unroll 1
                 for (int j = grp; j < kBlocksPerGroup; j += kTransformGroups) {

@@ -127,12 +127,12 @@ def test_default_path_takes_the_onchip_kernel_for_tall_products(mpk_lib, cuda, M
 
 
 @pytest.mark.parametrize("M,N,K,offset", [(512, 512, 2048, 1), (512, 512, 2048, 0), (384, 256, 1600, 0),
-                                          (256, 512, 4096, 8)])
+                                          (256, 512, 4096, 8), (512, 512, 1152, 0), (256, 768, 11008, 4)])
 def test_onchip_scale_byte_placement(whole_tiles, cuda, M, N, K, offset):
     """The on-chip kernel reads each row's A scale bytes 16 at a time when they are
-    16-byte aligned and K is a multiple of 512, else byte by byte: scales at an odd
-    or 8-byte offset and a K that is not a multiple of 512 give the same D as the
-    pre-pass path."""
+    16-byte aligned and K is a multiple of 512, 4 at a time when they are 4-byte
+    aligned and K is a multiple of 128 (the row's last group cut short), else byte by
+    byte: each placement gives the same D as the pre-pass path."""
     import torch
 
     mpk_lib = whole_tiles
