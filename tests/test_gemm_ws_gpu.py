@@ -98,11 +98,14 @@ def test_ws_exotic_scales_and_nan_codes(mpk_lib, cuda, with_nan):
     assert hist[0] + hist[1] >= 0.999 * sum(hist)
 
 
-@pytest.mark.parametrize("M,N,K", [(131072, 2048, 2048), (65536, 1024, 4096), (262144, 512, 1024)])
+@pytest.mark.parametrize("M,N,K", [(131072, 2048, 2048), (65536, 1024, 4096), (262144, 512, 1024),
+                                   (100003, 1000, 2048)])
 def test_default_path_takes_the_onchip_kernel_for_tall_products(mpk_lib, cuda, M, N, K):
     """Tall products with few columns go straight to the on-chip conversion kernel
     from the default entry point; D equals the pre-pass kernel's (caller workspace)
-    bit for bit, and the default call allocates no workspace."""
+    bit for bit, and the default call allocates no workspace.  The last shape has a
+    ragged last row tile, a partial last column chunk and C/D rows too short for
+    16-byte stores."""
     import torch
 
     g = torch.Generator(device="cuda").manual_seed(M + N + K)
@@ -111,7 +114,7 @@ def test_default_path_takes_the_onchip_kernel_for_tall_products(mpk_lib, cuda, M
     B = (torch.randn((K, N), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
     assert mpk_lib.gemm_path(Ad, B, M, N, K) == mpk_lib.PATH_ONCHIP
     D0 = torch.empty((M, N), dtype=torch.uint8, device="cuda")
-    S0 = torch.empty((M, N // 32), dtype=torch.uint8, device="cuda")
+    S0 = torch.empty((M, (N + 31) // 32), dtype=torch.uint8, device="cuda")
     mpk_lib.release_workspace_pool()
     torch.cuda.synchronize()
     free0 = torch.cuda.mem_get_info()[0]
