@@ -535,10 +535,12 @@ __device__ __noinline__ void convert_block_exact(const uint8_t* a8row, uint32_t 
 }
 
 // Fast path for one row of one K block (same contract as convert_block_exact),
-// valid when all four scale bytes are in 3..134, no code is NaN (0x7F/0xFF) and all
-// 128 codes are inside K: fast_block_ok checks this on the eight 16-code chunks
-// q[0..7], and convert_half_fast converts 32 codes (two chunks, one scale byte s)
-// to 16 words.
+// valid when the scale bytes of the 32-code blocks holding codes inside K are in
+// 3..134 and no code is NaN (0x7F/0xFF): fast_block_ok checks this on the eight
+// 16-code chunks q[0..7], and convert_half_fast converts 32 codes (two chunks, one
+// scale byte s) to 16 words.  Codes past K are zeros (the TMA load fills them), and
+// their scale bytes read 0 (2^-7 as a factor), so they convert to +0 as on the exact
+// path.
 // Each code's sign and 7 magnitude bits are moved into a BF16 bit pattern equal to
 // code x 2^-120 (the E4M3 exponent bits land in the low BF16 exponent bits; E4M3
 // subnormals become BF16 subnormals); one BF16 multiply by 2^(s-7) -- a power of
@@ -557,9 +559,10 @@ __device__ __forceinline__ bool fast_block_ok(const uint4 (&q)[OC_BK / 16], uint
 #pragma unroll
         for (int w = 0; w < 4; ++w) nan_probe |= (in[w] & 0x7F7F7F7Fu) + 0x01010101u;  // 0x7F -> 0x80
     }
-    bool ok = (nan_probe & 0x80808080u) == 0u && kvalid >= OC_BK;
+    bool ok = (nan_probe & 0x80808080u) == 0u;
 #pragma unroll
-    for (int b = 0; b < OC_BK / 32; ++b) ok = ok && (((scales >> (8 * b)) & 0xFFu) - 3u) <= 131u;
+    for (int b = 0; b < OC_BK / 32; ++b)
+        ok = ok && (32 * b >= kvalid || (((scales >> (8 * b)) & 0xFFu) - 3u) <= 131u);
     return ok;
 }
 
