@@ -597,12 +597,17 @@ def run_gemm_arm(args, world, rank, local, dist):
         if world > 1 and args.scaling == "strong" else None
 
     # Denominator: the burst cuBLAS figure, unless the clock record shows the power
-    # cap acting during the timed region, in which case the sustained figure (the
-    # same GEMM measured back to back under the cap).  Both fractions are reported.
+    # cap acting during the timed region -- the sw_power_cap reason set and the
+    # median SM clock below 95 % of its maximum -- in which case the sustained figure
+    # (the same GEMM measured back to back under the cap).  Both fractions are
+    # reported.
     peaks, peak_src = load_peaks()
     burst = float(peaks["bf16_tflops"])
     sustained = float(peaks.get("bf16_tflops_sustained", burst))
-    capped = "sw_power_cap" in clocks["reasons"]
+    med_mhz = (clocks.get("nvml") or {}).get("sm_mhz_median") or clocks.get("sm_mhz")
+    max_mhz = clocks.get("sm_max_mhz")
+    capped = "sw_power_cap" in clocks["reasons"] and (
+        med_mhz is None or not max_mhz or med_mhz < 0.95 * max_mhz)
     peak = sustained if capped else burst
     hbm = float(peaks["hbm_gbs"])
     pre_bytes = M * K + M * ((K + 31) // 32) + 2 * M * K
@@ -613,7 +618,9 @@ def run_gemm_arm(args, world, rank, local, dist):
                 "unit": "TFLOP/s", "frac": round(kernel_tflops / peak, 4),
                 "traffic": load_traffic(kernel_name, args.workload) if world == 1 else None,
                 "peak_source": (f"{peak_src} bf16_tflops_sustained (sw_power_cap active in the timed "
-                                f"region)" if capped else f"{peak_src} bf16_tflops (burst)"),
+                                f"region, SM clock median {med_mhz} of {max_mhz} MHz)" if capped
+                                else f"{peak_src} bf16_tflops (burst; SM clock median {med_mhz} of "
+                                     f"{max_mhz} MHz in the timed region)"),
                 "frac_of_burst": round(kernel_tflops / burst, 4),
                 "frac_of_sustained": round(kernel_tflops / sustained, 4),
                 "algorithmic": f"2*M*N*K = {flops:.4e} FLOP per launch (this GPU's slab {M}x{N}x{K})",
